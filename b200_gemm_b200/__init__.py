@@ -1,0 +1,156 @@
+"""b200_gemm_b200: bf16 GEMM (C = A . B^T, fp32 accumulate) for B200 / sm_100a.
+
+Python face of the C-ABI in include/b200gemm.h.  The reference project's
+interface is the C++ launcher runKernel1(M, N, K, A, B, C, DB)
+(b200_kernels/matmul_1.cuh:386) behind run_kernel(kernel_num, ...)
+(matmul_b200.cu:28-38); `run_kernel` below keeps that shape for Python
+callers, and `Gemm` exposes the handle-based API with streams and status.
+
+torch is used only for device memory and streams; all GEMM work happens in
+the hand-written sm_100a kernel of libb200gemm.so.  There is no CPU or
+library fallback: without the built library every call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+
+from . import _lib
+from ._lib import B200GemmError, strerror
+
+__all__ = ["Gemm", "gemm", "run_kernel", "schedule", "B200GemmError", "strerror", "version"]
+
+
+def version() -> int:
+    return _lib.load().b200gemm_version()
+
+
+def _ptr(t) -> int:
+    return 0 if t is None else int(t.data_ptr())
+
+
+def _stream_ptr(stream) -> int:
+    if stream is None:
+        import torch
+
+        return int(torch.cuda.current_stream().cuda_stream)
+    if isinstance(stream, int):
+        return stream
+    return int(stream.cuda_stream)
+
+
+class Gemm:
+    """A b200gemm handle bound to one CUDA device."""
+
+    def __init__(self, device: int = 0):
+        self._lib = _lib.load()
+        self.device = int(device)
+        h = ctypes.c_void_p()
+        _lib.check(self._lib.b200gemm_create(ctypes.byref(h), self.device), "b200gemm_create")
+        self._h = h
+
+    def close(self) -> None:
+        if getattr(self, "_h", None) is not None and self._h.value:
+            self._lib.b200gemm_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):  # pragma: no cover - interpreter shutdown order varies
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    # ------------------------------------------------------------------ raw
+    def bf16_nt_ptr(self, M: int, N: int, K: int, a_ptr: int, b_ptr: int, c_ptr: int, ldc: int,
+                    stream_ptr: int = 0) -> int:
+        """Raw pointer call; returns the status code (no exception)."""
+        return self._lib.b200gemm_bf16_nt(self._h, M, N, K, a_ptr, b_ptr, c_ptr, ldc, stream_ptr)
+
+    # --------------------------------------------------------------- tensors
+    def bf16_nt(self, A, B, out=None, stream=None):
+        """out[M, N] = A[M, K] @ B[N, K]^T for bf16 CUDA tensors.
+
+        `out` may be a column slice of a wider row-major matrix (stride(1) == 1);
+        its row stride is passed as ldc.
+        """
+        import torch
+
+        if A.dtype != torch.bfloat16 or B.dtype != torch.bfloat16:
+            raise TypeError("A and B must be torch.bfloat16")
+        if A.dim() != 2 or B.dim() != 2 or A.shape[1] != B.shape[1]:
+            raise ValueError(f"shape mismatch: A {tuple(A.shape)}, B {tuple(B.shape)}")
+        if A.stride(1) != 1 or B.stride(1) != 1 or A.stride(0) != A.shape[1] or B.stride(0) != B.shape[1]:
+            raise ValueError("A and B must be contiguous row-major (K-major)")
+        M, K = A.shape
+        N = B.shape[0]
+        if out is None:
+            out = torch.empty(M, N, device=A.device, dtype=torch.bfloat16)
+        if out.dtype != torch.bfloat16 or tuple(out.shape) != (M, N) or out.stride(1) != 1:
+            raise ValueError("out must be a bf16 [M, N] row-major view")
+        ldc = out.stride(0) if M > 1 else max(N, 8 * ((N + 7) // 8))
+        rc = self.bf16_nt_ptr(M, N, K, _ptr(A), _ptr(B), _ptr(out), ldc, _stream_ptr(stream))
+        _lib.check(rc, "b200gemm_bf16_nt")
+        return out
+
+    def last_device_status(self):
+        detail = (ctypes.c_uint * 4)()
+        rc = self._lib.b200gemm_last_device_status(self._h, detail)
+        return rc, list(detail)
+
+    def set_timeout_ns(self, ns: int) -> None:
+        _lib.check(self._lib.b200gemm_set_timeout_ns(self._h, int(ns)), "b200gemm_set_timeout_ns")
+
+    def selftest_watchdog(self, timeout_ns: int, stream=None) -> None:
+        rc = self._lib.b200gemm_selftest_watchdog(self._h, int(timeout_ns), _stream_ptr(stream))
+        _lib.check(rc, "b200gemm_selftest_watchdog")
+
+
+_handles: dict[int, Gemm] = {}
+_handles_lock = threading.Lock()
+
+
+def _handle_for(device: int) -> Gemm:
+    with _handles_lock:
+        h = _handles.get(device)
+        if h is None:
+            h = _handles[device] = Gemm(device)
+        return h
+
+
+def gemm(A, B, out=None, stream=None):
+    """out = A @ B^T (bf16, fp32 accumulate) on A's device."""
+    return _handle_for(A.device.index if A.device.index is not None else 0).bf16_nt(A, B, out, stream)
+
+
+def run_kernel(kernel_num: int, M: int, N: int, K: int, A, B, C) -> None:
+    """Mirror of the reference bench's dispatcher (matmul_b200.cu:28-38).
+
+    kernel 0: cuBLASLt through torch (the reference's cuBLAS comparator,
+              matmul_b200.cu:13-26, with the operand order fixed for
+              non-square shapes);
+    kernel 2: this library's sm_100a kernel (the C++ shim `runKernel2`).
+    A [M,K], B [N,K], C [M,N]: bf16 CUDA tensors.
+    """
+    import torch
+
+    if kernel_num == 0:
+        torch.matmul(A.view(M, K), B.view(N, K).t(), out=C.view(M, N))
+    elif kernel_num == 2:
+        rc = _lib.load().b200gemm_run_kernel(M, N, K, _ptr(A), _ptr(B), _ptr(C), None)
+        _lib.check(rc, "b200gemm_run_kernel")
+    else:
+        raise ValueError(f"kernel {kernel_num}: 0 = cuBLASLt, 2 = b200gemm")
+
+
+def schedule(tiles_m: int, tiles_n: int):
+    """Host copy of the kernel's tile order (list of (tile_m, tile_n))."""
+    n = tiles_m * tiles_n
+    buf = (ctypes.c_uint * n)()
+    _lib.check(_lib.load().b200gemm_schedule_host(tiles_m, tiles_n, buf), "b200gemm_schedule_host")
+    return [(v >> 16, v & 0xFFFF) for v in buf]

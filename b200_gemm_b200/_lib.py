@@ -1,0 +1,74 @@
+"""ctypes binding of the C-ABI declared in include/b200gemm.h.
+
+The shared library is built in-tree (b200_gemm_b200/lib/libb200gemm.so) by
+b200_gemm_b200/build.py.  There is no fallback: if the library is missing or
+does not load, every entry point raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "lib" / "libb200gemm.so"
+
+OK = 0
+ERR_INVALID_ARG = 1
+ERR_UNSUPPORTED = 2
+ERR_CUDA = 3
+ERR_DEVICE_TIMEOUT = 4
+ERR_NO_DEVICE = 5
+ERR_TOO_LARGE = 6
+
+_c_int, _c_uint, _c_ull, _vp = ctypes.c_int, ctypes.c_uint, ctypes.c_ulonglong, ctypes.c_void_p
+
+# name -> (restype, argtypes); one line per declaration in include/b200gemm.h
+SIGNATURES = {
+    "b200gemm_create": (_c_int, [ctypes.POINTER(_vp), _c_int]),
+    "b200gemm_destroy": (None, [_vp]),
+    "b200gemm_bf16_nt": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp, _vp, _vp, _c_int, _vp]),
+    "b200gemm_last_device_status": (_c_int, [_vp, ctypes.POINTER(_c_uint)]),
+    "b200gemm_set_timeout_ns": (_c_int, [_vp, _c_ull]),
+    "b200gemm_selftest_watchdog": (_c_int, [_vp, _c_ull, _vp]),
+    "b200gemm_run_kernel": (_c_int, [_c_int, _c_int, _c_int, _vp, _vp, _vp, ctypes.POINTER(_c_int)]),
+    "b200gemm_schedule_host": (_c_int, [_c_uint, _c_uint, ctypes.POINTER(_c_uint)]),
+    "b200gemm_strerror": (ctypes.c_char_p, [_c_int]),
+    "b200gemm_version": (_c_int, []),
+}
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+class B200GemmError(RuntimeError):
+    """A b200gemm entry point returned a non-zero status."""
+
+    def __init__(self, code: int, where: str):
+        self.code = code
+        super().__init__(f"{where}: {strerror(code)} (status {code})")
+
+
+def load() -> ctypes.CDLL:
+    """Load the library (once).  Raises if it is missing: there is no fallback."""
+    global _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                raise RuntimeError(
+                    f"{LIB_PATH} is missing; build it with `python -m b200_gemm_b200.build`")
+            lib = ctypes.CDLL(str(LIB_PATH))
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = lib
+        return _lib
+
+
+def strerror(code: int) -> str:
+    return load().b200gemm_strerror(int(code)).decode()
+
+
+def check(code: int, where: str) -> None:
+    if code != OK:
+        raise B200GemmError(code, where)

@@ -1,0 +1,397 @@
+// Host side of the C-ABI in include/b200gemm.h: argument validation, the
+// per-handle caches (tensor maps, tile schedules), device status words and
+// kernel launches.  Replaces the reference launcher runKernel1
+// (b200_kernels/matmul_1.cuh:386-418) and its hidden globals (:5-11).
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "b200gemm.h"
+#include "gemm_sm100.cuh"
+#include "schedule.cuh"
+
+namespace b200gemm {
+
+constexpr int kStages = 6;
+constexpr int kVersion = 10000;  // 1.0.0
+constexpr int kMapCacheSize = 8;
+constexpr size_t kScheduleCacheSize = 16;
+constexpr unsigned long long kDefaultTimeoutNs = 2000000000ull;
+
+using Layout = SmemLayout<kStages>;
+
+// Restores the caller's current device on scope exit.
+class DeviceGuard {
+ public:
+  explicit DeviceGuard(int device) {
+    ok_ = cudaGetDevice(&prev_) == cudaSuccess;
+    if (ok_ && prev_ != device) ok_ = cudaSetDevice(device) == cudaSuccess;
+    switched_ = ok_ && prev_ != device;
+  }
+  ~DeviceGuard() {
+    if (switched_) cudaSetDevice(prev_);
+  }
+  bool ok() const { return ok_; }
+
+ private:
+  int prev_ = 0;
+  bool ok_ = false;
+  bool switched_ = false;
+};
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+  });
+  return fn;
+}
+
+// Row-major bf16 matrix [outer x inner] with a row pitch in bytes, read or
+// written in boxes of [box_outer x box_inner] through the 128-byte swizzle.
+bool encode_2d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer,
+               uint64_t pitch_bytes, uint32_t box_inner, uint32_t box_outer) {
+  auto encode = tensor_map_encoder();
+  if (encode == nullptr) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {pitch_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t elem_strides[2] = {1, 1};
+  const CUresult r =
+      encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box,
+             elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+struct MapEntry {
+  bool valid = false;
+  const void* a = nullptr;
+  const void* b = nullptr;
+  void* c = nullptr;
+  int M = 0, N = 0, K = 0, ldc = 0;
+  uint64_t last_use = 0;
+  CUtensorMap map_a, map_b, map_c;
+};
+
+struct ScheduleEntry {
+  uint32_t tiles_m = 0, tiles_n = 0;
+  uint32_t* dev = nullptr;
+  uint64_t last_use = 0;
+};
+
+int set_gemm_attributes() {
+  const cudaError_t e = cudaFuncSetAttribute(gemm_bf16_nt_sm100<kStages>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             Layout::kBytes);
+  return e == cudaSuccess ? B200GEMM_OK : B200GEMM_ERR_CUDA;
+}
+
+}  // namespace b200gemm
+
+using namespace b200gemm;
+
+struct b200gemm_handle {
+  int device = 0;
+  int sm_count = 0;
+  int max_clusters = 0;  // co-resident 2-CTA clusters of the GEMM kernel
+  unsigned int* status_dev = nullptr;
+  unsigned long long timeout_ns = kDefaultTimeoutNs;
+  std::mutex mu;
+  uint64_t tick = 0;
+  MapEntry maps[kMapCacheSize];
+  std::vector<ScheduleEntry> schedules;
+};
+
+extern "C" int b200gemm_version(void) { return kVersion; }
+
+extern "C" const char* b200gemm_strerror(int code) {
+  switch (code) {
+    case B200GEMM_OK: return "ok";
+    case B200GEMM_ERR_INVALID_ARG: return "invalid argument (null handle or pointer, negative size)";
+    case B200GEMM_ERR_UNSUPPORTED:
+      return "unsupported layout (needs K % 8 == 0, ldc % 8 == 0, ldc >= N, 16-byte aligned pointers)";
+    case B200GEMM_ERR_CUDA: return "a CUDA runtime or driver call failed";
+    case B200GEMM_ERR_DEVICE_TIMEOUT: return "a bounded wait inside a kernel ran out of time";
+    case B200GEMM_ERR_NO_DEVICE: return "no such CUDA device, or the device is not sm_100";
+    case B200GEMM_ERR_TOO_LARGE: return "a dimension exceeds the supported range";
+    default: return "unknown status code";
+  }
+}
+
+extern "C" int b200gemm_create(b200gemm_t* out, int device) {
+  if (out == nullptr) return B200GEMM_ERR_INVALID_ARG;
+  *out = nullptr;
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || device < 0 || device >= count) {
+    cudaGetLastError();
+    return B200GEMM_ERR_NO_DEVICE;
+  }
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return B200GEMM_ERR_CUDA;
+  if (prop.major != 10 || prop.minor != 0) return B200GEMM_ERR_NO_DEVICE;
+  DeviceGuard guard(device);
+  if (!guard.ok()) return B200GEMM_ERR_CUDA;
+  if (set_gemm_attributes() != B200GEMM_OK) return B200GEMM_ERR_CUDA;
+  if (tensor_map_encoder() == nullptr) return B200GEMM_ERR_CUDA;
+
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(prop.multiProcessorCount & ~1, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = Layout::kBytes;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, gemm_bf16_nt_sm100<kStages>, &cfg) != cudaSuccess ||
+      clusters <= 0) {
+    cudaGetLastError();
+    return B200GEMM_ERR_CUDA;
+  }
+
+  auto* h = new b200gemm_handle();
+  h->device = device;
+  h->sm_count = prop.multiProcessorCount;
+  h->max_clusters = clusters;
+  if (cudaMalloc(&h->status_dev, 4 * sizeof(unsigned int)) != cudaSuccess ||
+      cudaMemset(h->status_dev, 0, 4 * sizeof(unsigned int)) != cudaSuccess) {
+    cudaFree(h->status_dev);
+    delete h;
+    return B200GEMM_ERR_CUDA;
+  }
+  *out = h;
+  return B200GEMM_OK;
+}
+
+extern "C" void b200gemm_destroy(b200gemm_t h) {
+  if (h == nullptr) return;
+  {
+    DeviceGuard guard(h->device);
+    cudaDeviceSynchronize();
+    for (auto& s : h->schedules) cudaFree(s.dev);
+    cudaFree(h->status_dev);
+  }
+  delete h;
+}
+
+extern "C" int b200gemm_set_timeout_ns(b200gemm_t h, unsigned long long timeout_ns) {
+  if (h == nullptr) return B200GEMM_ERR_INVALID_ARG;
+  std::lock_guard<std::mutex> lock(h->mu);
+  h->timeout_ns = timeout_ns;
+  return B200GEMM_OK;
+}
+
+namespace {
+
+// Tile schedule for a (tiles_m x tiles_n) grid, built on the device the
+// first time the grid is seen and cached in the handle.  Caller holds h->mu.
+int schedule_for(b200gemm_t h, uint32_t tiles_m, uint32_t tiles_n, cudaStream_t stream,
+                 const uint32_t** out) {
+  for (auto& s : h->schedules) {
+    if (s.tiles_m == tiles_m && s.tiles_n == tiles_n) {
+      s.last_use = ++h->tick;
+      *out = s.dev;
+      return B200GEMM_OK;
+    }
+  }
+  if (h->schedules.size() >= kScheduleCacheSize) {
+    size_t victim = 0;
+    for (size_t i = 1; i < h->schedules.size(); ++i)
+      if (h->schedules[i].last_use < h->schedules[victim].last_use) victim = i;
+    cudaFree(h->schedules[victim].dev);  // synchronises the device
+    h->schedules.erase(h->schedules.begin() + static_cast<long>(victim));
+  }
+  ScheduleEntry e;
+  e.tiles_m = tiles_m;
+  e.tiles_n = tiles_n;
+  const size_t bytes = static_cast<size_t>(tiles_m) * tiles_n * sizeof(uint32_t);
+  if (cudaMalloc(&e.dev, bytes) != cudaSuccess) return B200GEMM_ERR_CUDA;
+  build_hilbert_schedule_kernel<<<1, 1024, 0, stream>>>(tiles_m, tiles_n, e.dev);
+  // Wait once so the table is valid for launches on any stream.
+  if (cudaGetLastError() != cudaSuccess || cudaStreamSynchronize(stream) != cudaSuccess) {
+    cudaFree(e.dev);
+    return B200GEMM_ERR_CUDA;
+  }
+  e.last_use = ++h->tick;
+  h->schedules.push_back(e);
+  *out = e.dev;
+  return B200GEMM_OK;
+}
+
+// Tensor maps for one argument tuple, cached in the handle.  Caller holds h->mu.
+int maps_for(b200gemm_t h, int M, int N, int K, const void* A, const void* B, void* C, int ldc,
+             CUtensorMap* ma, CUtensorMap* mb, CUtensorMap* mc) {
+  MapEntry* slot = nullptr;
+  for (auto& m : h->maps) {
+    if (m.valid && m.a == A && m.b == B && m.c == C && m.M == M && m.N == N && m.K == K &&
+        m.ldc == ldc) {
+      slot = &m;
+      break;
+    }
+  }
+  if (slot == nullptr) {
+    slot = &h->maps[0];
+    for (auto& m : h->maps) {
+      if (!m.valid) {
+        slot = &m;
+        break;
+      }
+      if (m.last_use < slot->last_use) slot = &m;
+    }
+    slot->valid = false;
+    const uint64_t k = static_cast<uint64_t>(K);
+    if (!encode_2d(&slot->map_a, A, k, static_cast<uint64_t>(M), k * 2, kBlockK, 128) ||
+        !encode_2d(&slot->map_b, B, k, static_cast<uint64_t>(N), k * 2, kBlockK, 128) ||
+        !encode_2d(&slot->map_c, C, static_cast<uint64_t>(N), static_cast<uint64_t>(M),
+                   static_cast<uint64_t>(ldc) * 2, kCBoxCols, kCBoxRows)) {
+      return B200GEMM_ERR_CUDA;
+    }
+    slot->a = A;
+    slot->b = B;
+    slot->c = C;
+    slot->M = M;
+    slot->N = N;
+    slot->K = K;
+    slot->ldc = ldc;
+    slot->valid = true;
+  }
+  slot->last_use = ++h->tick;
+  *ma = slot->map_a;
+  *mb = slot->map_b;
+  *mc = slot->map_c;
+  return B200GEMM_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+extern "C" int b200gemm_bf16_nt(b200gemm_t h, int M, int N, int K, const void* A, const void* B,
+                                void* C, int ldc, void* stream_ptr) {
+  if (h == nullptr || M < 0 || N < 0 || K < 0) return B200GEMM_ERR_INVALID_ARG;
+  if (M == 0 || N == 0) return B200GEMM_OK;
+  if (C == nullptr || (K > 0 && (A == nullptr || B == nullptr))) return B200GEMM_ERR_INVALID_ARG;
+  if (ldc < N || (ldc % 8) != 0 || (K % 8) != 0) return B200GEMM_ERR_UNSUPPORTED;
+  if (!aligned16(C) || (K > 0 && (!aligned16(A) || !aligned16(B)))) return B200GEMM_ERR_UNSUPPORTED;
+  const uint32_t tiles_m = static_cast<uint32_t>((M + kTileM - 1) / kTileM);
+  const uint32_t tiles_n = static_cast<uint32_t>((N + kTileN - 1) / kTileN);
+  if (tiles_m > 0xFFFFu || tiles_n > 0xFFFFu ||
+      static_cast<uint64_t>(tiles_m) * tiles_n > 0x7FFFFFFFull) {
+    return B200GEMM_ERR_TOO_LARGE;
+  }
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  DeviceGuard guard(h->device);
+  if (!guard.ok()) return B200GEMM_ERR_CUDA;
+
+  if (K == 0) {  // empty sum: C = 0
+    return cudaMemset2DAsync(C, static_cast<size_t>(ldc) * 2, 0, static_cast<size_t>(N) * 2,
+                             static_cast<size_t>(M), stream) == cudaSuccess
+               ? B200GEMM_OK
+               : B200GEMM_ERR_CUDA;
+  }
+
+  CUtensorMap ma, mb, mc;
+  const uint32_t* sched = nullptr;
+  unsigned long long timeout_ns;
+  {
+    std::lock_guard<std::mutex> lock(h->mu);
+    int rc = schedule_for(h, tiles_m, tiles_n, stream, &sched);
+    if (rc != B200GEMM_OK) return rc;
+    rc = maps_for(h, M, N, K, A, B, C, ldc, &ma, &mb, &mc);
+    if (rc != B200GEMM_OK) return rc;
+    timeout_ns = h->timeout_ns;
+  }
+
+  GemmParams p;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.num_kb = (K + kBlockK - 1) / kBlockK;
+  p.num_tiles = static_cast<int>(tiles_m * tiles_n);
+  p.tiles = sched;
+  p.status = h->status_dev;
+  p.timeout_ns = timeout_ns;
+
+  const int clusters = p.num_tiles < h->max_clusters ? p.num_tiles : h->max_clusters;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * clusters), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = Layout::kBytes;
+  cfg.stream = stream;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_bf16_nt_sm100<kStages>, ma, mb, mc, p);
+  return e == cudaSuccess ? B200GEMM_OK : B200GEMM_ERR_CUDA;
+}
+
+extern "C" int b200gemm_last_device_status(b200gemm_t h, unsigned int* detail) {
+  if (h == nullptr) return B200GEMM_ERR_INVALID_ARG;
+  DeviceGuard guard(h->device);
+  if (!guard.ok()) return B200GEMM_ERR_CUDA;
+  unsigned int words[4] = {0, 0, 0, 0};
+  if (cudaDeviceSynchronize() != cudaSuccess ||
+      cudaMemcpy(words, h->status_dev, sizeof(words), cudaMemcpyDeviceToHost) != cudaSuccess ||
+      cudaMemset(h->status_dev, 0, sizeof(words)) != cudaSuccess) {
+    return B200GEMM_ERR_CUDA;
+  }
+  if (detail != nullptr) std::memcpy(detail, words, sizeof(words));
+  return words[0] == 0 ? B200GEMM_OK : static_cast<int>(words[0]);
+}
+
+extern "C" int b200gemm_selftest_watchdog(b200gemm_t h, unsigned long long timeout_ns,
+                                          void* stream_ptr) {
+  if (h == nullptr) return B200GEMM_ERR_INVALID_ARG;
+  DeviceGuard guard(h->device);
+  if (!guard.ok()) return B200GEMM_ERR_CUDA;
+  watchdog_selftest_kernel<<<2, 32, 0, static_cast<cudaStream_t>(stream_ptr)>>>(h->status_dev,
+                                                                               timeout_ns);
+  return cudaGetLastError() == cudaSuccess ? B200GEMM_OK : B200GEMM_ERR_CUDA;
+}
+
+extern "C" int b200gemm_schedule_host(unsigned int tiles_m, unsigned int tiles_n,
+                                      unsigned int* out) {
+  if (out == nullptr || tiles_m == 0 || tiles_n == 0 || tiles_m > 0xFFFFu || tiles_n > 0xFFFFu)
+    return B200GEMM_ERR_INVALID_ARG;
+  const uint32_t side = hilbert_side(tiles_m, tiles_n);
+  const uint64_t cells = static_cast<uint64_t>(side) * side;
+  uint64_t w = 0;
+  for (uint64_t d = 0; d < cells; ++d) {
+    uint32_t x, y;
+    hilbert_cell(side, static_cast<uint32_t>(d), x, y);
+    if (x < tiles_m && y < tiles_n) out[w++] = pack_tile(x, y);
+  }
+  return B200GEMM_OK;
+}
+
+extern "C" int b200gemm_run_kernel(int M, int N, int K, const void* A, const void* B, void* C,
+                                   int* DB) {
+  (void)DB;
+  static std::mutex mu;
+  static b200gemm_t handles[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return B200GEMM_ERR_NO_DEVICE;
+  b200gemm_t h;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (handles[dev] == nullptr) {
+      const int rc = b200gemm_create(&handles[dev], dev);
+      if (rc != B200GEMM_OK) return rc;
+    }
+    h = handles[dev];
+  }
+  return b200gemm_bf16_nt(h, M, N, K, A, B, C, N, nullptr);
+}

@@ -1,0 +1,333 @@
+// Persistent, warp-specialised bf16 GEMM for sm_100a:
+//   C[M x N] (bf16, row-major, leading dim ldc) = A[M x K] . B[N x K]^T
+// with A and B row-major ("K-major") bf16 and fp32 accumulation in TMEM.
+//
+// Reference path: b200_kernels/matmul_1.cuh:329-381 (`matmulKernel1`) and
+// its helpers (tma_warp :158-196, mma_warp :209-261, epilogue :270-319).
+// Same contract and the same per-pair MMA tile (256 x 256, K step 16,
+// cta_group::2); the pipeline around it is rebuilt:
+//   * the smem ring is initialised once and runs across tiles (the
+//     reference re-initialises every barrier and cluster-syncs per tile,
+//     matmul_1.cuh:373-374);
+//   * two TMEM accumulators (2 x 256 fp32 columns) let the MMA warp start
+//     tile i+1 while four dedicated epilogue warps drain tile i;
+//   * the epilogue reads 32 columns per tcgen05.ld, converts to bf16 (RNE),
+//     writes 128B-swizzled staging buffers (bank-conflict free) and streams
+//     them out with per-warp TMA stores, double-buffered;
+//   * ragged M, N and K (K % 8 == 0) are handled by TMA bounds (zero fill on
+//     loads, clipping on stores) instead of requiring multiples of 256/64;
+//   * every wait is bounded (see ptx_sm100.cuh).
+//
+// Warp roles (192 threads per CTA, one CTA per SM, clusters of 2 CTAs):
+//   warp 0      TMA producer (one lane), both CTAs
+//   warp 1      MMA issuer (one lane), leader CTA only; TMEM allocator
+//   warps 2..5  epilogue; warp w reads TMEM lanes 32*(w%4) .. +31
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+
+#include "ptx_sm100.cuh"
+
+namespace b200gemm {
+
+constexpr int kTileM = 256;   // rows of C per CTA pair (128 per CTA)
+constexpr int kTileN = 256;   // columns of C per CTA pair (= MMA N)
+constexpr int kBlockK = 64;   // K per pipeline stage: one 128-byte swizzle row of bf16
+constexpr int kMmaK = 16;     // K per tcgen05.mma (kind::f16)
+constexpr int kThreads = 192;
+constexpr int kAccCols = 256;     // fp32 TMEM columns per accumulator
+constexpr int kTmemCols = 512;    // two accumulators
+constexpr int kStageBytesA = 128 * kBlockK * 2;  // per CTA per stage
+constexpr int kStageBytesB = 128 * kBlockK * 2;  // per CTA per stage (half of the pair's 256 rows)
+constexpr int kCBoxCols = 64;     // one 128-byte row of bf16
+constexpr int kCBoxRows = 32;     // one warp's TMEM lane quarter
+constexpr int kCStageBytes = kCBoxCols * kCBoxRows * 2;
+constexpr int kEpilogueWarps = 4;
+
+// Watchdog sites (reported in status word 1).
+enum : unsigned int {
+  kSiteProducer = 1,
+  kSiteMmaTmemEmpty = 2,
+  kSiteMmaFull = 3,
+  kSiteEpilogue = 4,
+  kSiteDrain = 5,
+  kSiteSelftest = 9,
+};
+
+struct GemmParams {
+  int M, N, K;
+  int num_kb;                 // ceil(K / kBlockK)
+  int num_tiles;              // ceil(M/256) * ceil(N/256)
+  const uint32_t* tiles;      // schedule: num_tiles packed (tm << 16 | tn) in curve order
+  unsigned int* status;       // 4 status words (code, site, cta, tile); may be null
+  unsigned long long timeout_ns;
+};
+
+template <int STAGES>
+struct SmemLayout {
+  static constexpr int kA = 0;
+  static constexpr int kB = kA + STAGES * kStageBytesA;
+  static constexpr int kC = kB + STAGES * kStageBytesB;
+  static constexpr int kFull = kC + kEpilogueWarps * 2 * kCStageBytes;
+  static constexpr int kEmpty = kFull + 8 * STAGES;
+  static constexpr int kTFull = kEmpty + 8 * STAGES;
+  static constexpr int kTEmpty = kTFull + 16;
+  static constexpr int kDrain = kTEmpty + 16;
+  static constexpr int kTmemSlot = kDrain + 8;
+  static constexpr int kAbort = kTmemSlot + 4;
+  static constexpr int kEnd = kAbort + 4;
+  static constexpr int kBytes = kEnd + 1024;  // slack to align the base to 1024 B
+  static_assert(kBytes <= 232448, "exceeds the 227 KB per-CTA shared memory limit");
+};
+
+// Instruction descriptor, kind::f16: D = f32, A = B = bf16, both K-major,
+// M = 256 (pair), N = 256.
+constexpr uint32_t kIdescBf16 = (1u << 4)            // D format f32
+                                | (1u << 7)          // A format bf16
+                                | (1u << 10)         // B format bf16
+                                | ((kTileN >> 3) << 17) | ((kTileM >> 4) << 24);
+
+// Shared-memory matrix descriptor fields above the start address for a
+// K-major operand in the 128-byte swizzle layout written by TMA: 8-row groups
+// 1024 B apart (SBO), descriptor version 1, swizzle mode 2 (128 B).
+constexpr uint64_t kSmemDescHi = (uint64_t(1024 >> 4) << 32) | (uint64_t(1) << 16)  // LBO unused
+                                 | (uint64_t(1) << 46) | (uint64_t(2) << 61);
+
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
+  return kSmemDescHi | uint64_t((addr & 0x3FFFFu) >> 4);
+}
+
+template <int STAGES>
+__global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
+    gemm_bf16_nt_sm100(const __grid_constant__ CUtensorMap map_a,
+                       const __grid_constant__ CUtensorMap map_b,
+                       const __grid_constant__ CUtensorMap map_c, const GemmParams p) {
+  using L = SmemLayout<STAGES>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  const uint32_t raw = ptx::smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+  const uint32_t rank = ptx::cluster_ctarank();
+  const bool leader = (rank == 0);
+  const uint32_t cluster = ptx::cluster_id_x();
+  const uint32_t nclusters = ptx::num_clusters_x();
+
+  const uint32_t sA = base + L::kA, sB = base + L::kB, sC = base + L::kC;
+  const uint32_t full0 = base + L::kFull, empty0 = base + L::kEmpty;
+  const uint32_t tfull0 = base + L::kTFull, tempty0 = base + L::kTEmpty;
+  const uint32_t drain = base + L::kDrain, tmem_slot = base + L::kTmemSlot;
+
+  ptx::Watchdog wd;
+  wd.abort_flag = base + L::kAbort;
+  wd.peer_abort_flag = ptx::mapa(wd.abort_flag, rank ^ 1u);
+  wd.status = p.status;
+  wd.timeout_ns = p.timeout_ns;
+
+  if (threadIdx.x == 0) {
+    asm volatile("st.shared.u32 [%0], 0;" ::"r"(wd.abort_flag) : "memory");
+    for (int s = 0; s < STAGES; ++s) {
+      ptx::mbar_init(full0 + 8 * s, 1);   // leader's expect_tx arrival (+ bytes of both CTAs)
+      ptx::mbar_init(empty0 + 8 * s, 1);  // one MMA commit
+    }
+    for (int a = 0; a < 2; ++a) {
+      ptx::mbar_init(tfull0 + 8 * a, 1);                    // one MMA commit
+      ptx::mbar_init(tempty0 + 8 * a, 2 * kEpilogueWarps);  // every epilogue warp of the pair
+    }
+    ptx::mbar_init(drain, 1);
+    ptx::fence_mbar_init_cluster();
+    ptx::prefetch_tensormap(&map_a);
+    ptx::prefetch_tensormap(&map_b);
+    ptx::prefetch_tensormap(&map_c);
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc_cg2(tmem_slot, kTmemCols);
+    ptx::tmem_relinquish_cg2();
+  }
+  ptx::tc_fence_before();
+  ptx::cluster_sync_all();
+  ptx::tc_fence_after();
+  uint32_t tmem_base;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(tmem_base) : "r"(tmem_slot) : "memory");
+
+  const uint32_t num_tiles = static_cast<uint32_t>(p.num_tiles);
+  const int num_kb = p.num_kb;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint64_t policy = ptx::policy_evict_normal();
+      const uint32_t full_leader0 = ptx::mapa(full0, 0);
+      uint32_t stage = 0, phase = 0;
+      bool ok = true;
+      uint32_t next = (cluster < num_tiles) ? __ldg(p.tiles + cluster) : 0u;
+      for (uint32_t t = cluster; t < num_tiles && ok; t += nclusters) {
+        const uint32_t tile = next;
+        if (t + nclusters < num_tiles) next = __ldg(p.tiles + t + nclusters);
+        const int row_a = static_cast<int>(tile >> 16) * kTileM + static_cast<int>(rank) * 128;
+        const int row_b = static_cast<int>(tile & 0xFFFFu) * kTileN + static_cast<int>(rank) * 128;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!ptx::mbar_wait(empty0 + 8 * stage, phase ^ 1u, wd, kSiteProducer, t)) {
+            ok = false;
+            break;
+          }
+          if (leader) ptx::mbar_arrive_expect_tx(full0 + 8 * stage, 2 * (kStageBytesA + kStageBytesB));
+          const uint32_t fb = full_leader0 + 8 * stage;
+          ptx::tma_load_2d_cg2(sA + stage * kStageBytesA, &map_a, fb, kb * kBlockK, row_a, policy);
+          ptx::tma_load_2d_cg2(sB + stage * kStageBytesB, &map_b, fb, kb * kBlockK, row_b, policy);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ----------------------------------------------------------------- MMA
+    if (leader && lane == 0) {
+      const uint32_t own_empty0 = ptx::mapa(empty0, 0), peer_empty0 = ptx::mapa(empty0, 1);
+      const uint32_t own_tfull0 = ptx::mapa(tfull0, 0), peer_tfull0 = ptx::mapa(tfull0, 1);
+      uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+      bool ok = true;
+      for (uint32_t t = cluster; t < num_tiles && ok; t += nclusters) {
+        if (!ptx::mbar_wait(tempty0 + 8 * acc, acc_phase ^ 1u, wd, kSiteMmaTmemEmpty, t)) break;
+        ptx::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * kAccCols;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!ptx::mbar_wait(full0 + 8 * stage, phase, wd, kSiteMmaFull, t)) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          const uint64_t a_desc = smem_desc(sA + stage * kStageBytesA);
+          const uint64_t b_desc = smem_desc(sB + stage * kStageBytesB);
+#pragma unroll
+          for (int k = 0; k < kBlockK / kMmaK; ++k) {
+            // +32 bytes per K step inside the 128-byte swizzle row.
+            ptx::mma_bf16_cg2(d_tmem, a_desc + 2 * k, b_desc + 2 * k, kIdescBf16,
+                              (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          ptx::mma_commit_cg2(own_empty0 + 8 * stage);
+          ptx::mma_commit_cg2(peer_empty0 + 8 * stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        ptx::mma_commit_cg2(own_tfull0 + 8 * acc);
+        ptx::mma_commit_cg2(peer_tfull0 + 8 * acc);
+        acc ^= 1u;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      // Every MMA this thread issued must be complete before TMEM is freed
+      // and before the peer CTA (whose shared memory the MMAs read) exits.
+      ptx::mma_commit_cg2(ptx::mapa(drain, 0));
+      ptx::Watchdog dwd = wd;
+      dwd.timeout_ns = 100000000ull;  // 100 ms: independent of the caller's budget
+      ptx::mbar_wait_drain(drain, 0, dwd, kSiteDrain);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const uint32_t quarter = warp & 3u;  // TMEM lanes this warp may access
+    const uint32_t cstage0 = sC + (warp - 2u) * 2u * kCStageBytes;
+    const uint32_t tempty_leader0 = ptx::mapa(tempty0, 0);
+    uint32_t acc = 0, acc_phase = 0, cbuf = 0;
+    uint32_t next = (cluster < num_tiles) ? __ldg(p.tiles + cluster) : 0u;
+    for (uint32_t t = cluster; t < num_tiles; t += nclusters) {
+      const uint32_t tile = next;
+      if (t + nclusters < num_tiles) next = __ldg(p.tiles + t + nclusters);
+      const bool full_ok = ptx::mbar_wait(tfull0 + 8 * acc, acc_phase, wd, kSiteEpilogue, t);
+      if (!__all_sync(0xFFFFFFFFu, full_ok)) break;  // keep the warp's decision uniform
+      ptx::tc_fence_after();
+      const int row = static_cast<int>(tile >> 16) * kTileM + static_cast<int>(rank) * 128 +
+                      static_cast<int>(quarter) * 32;
+      const int col0 = static_cast<int>(tile & 0xFFFFu) * kTileN;
+      const uint32_t t_row = tmem_base + ((quarter * 32u) << 16) + acc * kAccCols;
+#pragma unroll 1
+      for (int c = 0; c < kTileN / kCBoxCols; ++c) {
+        uint32_t v0[32], v1[32];
+        ptx::tmem_ld_32x32b_x32(t_row + c * kCBoxCols, v0);
+        ptx::tmem_ld_32x32b_x32(t_row + c * kCBoxCols + 32, v1);
+        ptx::tmem_wait_ld();
+        if (c == kTileN / kCBoxCols - 1) {
+          // Whole accumulator is in registers: hand it back to the MMA warp.
+          ptx::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive_cluster(tempty_leader0 + 8 * acc);
+        }
+        uint32_t pk[32];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) pk[i] = ptx::pack_bf16x2(v0[2 * i], v0[2 * i + 1]);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) pk[16 + i] = ptx::pack_bf16x2(v1[2 * i], v1[2 * i + 1]);
+        const int col = col0 + c * kCBoxCols;
+        const bool store = (row < p.M) && (col < p.N);  // warp-uniform
+        if (store) {
+          const uint32_t buf = cstage0 + cbuf * kCStageBytes;
+          // The TMA store that last read this buffer (two stores ago) must be done reading.
+          if (lane == 0) ptx::bulk_wait_group_read<1>();
+          __syncwarp();
+          const uint32_t rowaddr = buf + lane * 128u;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            ptx::st_shared_v4(rowaddr + ((static_cast<uint32_t>(j) ^ (lane & 7u)) << 4), pk[4 * j],
+                              pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+          }
+          ptx::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            ptx::tma_store_2d(&map_c, buf, col, row);
+            ptx::bulk_commit_group();
+          }
+          cbuf ^= 1u;
+        }
+      }
+      acc ^= 1u;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+    if (lane == 0) ptx::bulk_wait_group<0>();
+    __syncwarp();
+  }
+
+  // --------------------------------------------------------------- teardown
+  if (threadIdx.x == 0 && ptx::aborted(wd)) {
+    // Let TMA loads that were issued but never consumed land before exit.
+    ptx::sleep_ns_bounded(200000ull);
+  }
+  ptx::tc_fence_before();
+  ptx::cluster_sync_all();
+  ptx::tc_fence_after();
+  if (warp == 1) ptx::tmem_dealloc_cg2(tmem_base, kTmemCols);
+}
+
+// Self-test of the watchdog: every CTA waits on an mbarrier that nothing
+// ever arrives on.  The bounded wait must give up after `timeout_ns`, record
+// kStatusTimeout and let the kernel exit normally.
+__global__ void __launch_bounds__(32, 1) __cluster_dims__(2, 1, 1)
+    watchdog_selftest_kernel(unsigned int* status, unsigned long long timeout_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ uint32_t abort_word;
+  const uint32_t rank = ptx::cluster_ctarank();
+  ptx::Watchdog wd;
+  wd.abort_flag = ptx::smem_u32(&abort_word);
+  wd.peer_abort_flag = ptx::mapa(wd.abort_flag, rank ^ 1u);
+  wd.status = status;
+  wd.timeout_ns = timeout_ns;
+  if (threadIdx.x == 0) {
+    abort_word = 0;
+    ptx::mbar_init(ptx::smem_u32(&bar), 1);
+    ptx::fence_mbar_init_cluster();
+  }
+  ptx::cluster_sync_all();
+  if (threadIdx.x == 0) {
+    ptx::mbar_wait(ptx::smem_u32(&bar), 0, wd, kSiteSelftest, 0);
+  }
+  __syncwarp();
+  ptx::cluster_sync_all();
+}
+
+}  // namespace b200gemm

@@ -1,0 +1,96 @@
+/*
+ * b200gemm: bf16 x bf16 -> bf16 GEMM (fp32 accumulate) for NVIDIA B200
+ * (sm_100a), C = A . B^T with
+ *   A: M x K, row-major (K contiguous, leading dimension K)
+ *   B: N x K, row-major (K contiguous, leading dimension K)
+ *   C: M x N, row-major, leading dimension ldc >= N
+ * Output elements are the fp32 sums rounded to bf16 (round to nearest even).
+ *
+ * This header is the drop-in boundary for the reference project's launcher
+ *   void runKernel1(int M, int N, int K, bf16 *A, bf16 *B, bf16 *C, int *DB)
+ *   (b200_kernels/matmul_1.cuh:386-418, exported at :422, dispatched from
+ *    run_kernel() in matmul_b200.cu:28-38).
+ * Differences from that launcher, all in the caller's favour: explicit
+ * stream, status codes instead of exit(1) (reference include/utils.cuh:13-20),
+ * a per-handle descriptor cache keyed on every argument (the reference keys
+ * its cache on M only, matmul_1.cuh:390), any M, N >= 0 and K % 8 == 0
+ * (the reference needs K % 64 == 0 and full 256 x 256 tiles).
+ *
+ * All entry points are thread-safe per handle.  Plain C types only.
+ */
+#ifndef B200GEMM_H_
+#define B200GEMM_H_
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define B200GEMM_OK 0
+#define B200GEMM_ERR_INVALID_ARG 1   /* null handle/pointer, negative size      */
+#define B200GEMM_ERR_UNSUPPORTED 2   /* K % 8, ldc % 8, ldc < N, misaligned ptr  */
+#define B200GEMM_ERR_CUDA 3          /* a CUDA runtime/driver call failed        */
+#define B200GEMM_ERR_DEVICE_TIMEOUT 4 /* a bounded wait inside a kernel ran out   */
+#define B200GEMM_ERR_NO_DEVICE 5     /* device missing or not sm_100             */
+#define B200GEMM_ERR_TOO_LARGE 6     /* a dimension exceeds the supported range  */
+
+typedef struct b200gemm_handle* b200gemm_t;
+
+/* Create a handle bound to CUDA device `device`.  Allocates a few bytes of
+ * device memory for the status words.  Replaces the reference's hidden
+ * globals d_tma_map_A/B/C, _prev_m/n/k and _dspace (matmul_1.cuh:5-11). */
+int b200gemm_create(b200gemm_t* handle, int device);
+
+/* Release the handle and every device buffer it owns. */
+void b200gemm_destroy(b200gemm_t handle);
+
+/* C = A . B^T (see top of file).  Asynchronous on `stream` (a cudaStream_t,
+ * NULL = legacy default stream).  A, B, C must be 16-byte aligned device
+ * pointers on the handle's device; K % 8 == 0; ldc % 8 == 0; ldc >= N.
+ * The first call for a new (M, N) tile grid builds the tile schedule and
+ * waits for it (one-time, per handle).
+ * Replaces runKernel1 (matmul_1.cuh:386-418). */
+int b200gemm_bf16_nt(b200gemm_t handle, int M, int N, int K, const void* A, const void* B,
+                     void* C, int ldc, void* stream);
+
+/* Waits for the handle's device, returns the first device-side error the
+ * kernels recorded since the last call (B200GEMM_OK or
+ * B200GEMM_ERR_DEVICE_TIMEOUT) and clears it.  `detail`, if non-null,
+ * receives 4 words: code, site, CTA id, tile index.
+ * No reference counterpart (its waits spin forever, b200_utils.cuh:451-463). */
+int b200gemm_last_device_status(b200gemm_t handle, unsigned int* detail);
+
+/* Budget for every bounded wait inside the kernels, in nanoseconds
+ * (default 2e9).  No reference counterpart. */
+int b200gemm_set_timeout_ns(b200gemm_t handle, unsigned long long timeout_ns);
+
+/* Launch a two-CTA kernel whose only wait can never be satisfied, with the
+ * given budget; afterwards b200gemm_last_device_status() must report
+ * B200GEMM_ERR_DEVICE_TIMEOUT.  Exercises the watchdog without a fault.
+ * No reference counterpart. */
+int b200gemm_selftest_watchdog(b200gemm_t handle, unsigned long long timeout_ns, void* stream);
+
+/* Drop-in for the reference launcher signature (matmul_1.cuh:386): uses a
+ * process-wide handle for the current device, the legacy default stream and
+ * ldc = N.  `DB` (the reference's debug buffer, unused by its B200 path,
+ * matmul_b200.cu:35) is accepted and ignored. */
+int b200gemm_run_kernel(int M, int N, int K, const void* A, const void* B, void* C, int* DB);
+
+/* Host computation of the persistent tile schedule the kernel follows for a
+ * tiles_m x tiles_n grid of 256 x 256 output tiles: out[0 .. tiles_m*tiles_n)
+ * receives (tile_m << 16 | tile_n) in Hilbert-curve order; entry j runs on
+ * cluster j mod (number of clusters).  The device builds the identical table.
+ * Replaces createHilbert (include/hilbert.hpp:42-84).  Needs no GPU. */
+int b200gemm_schedule_host(unsigned int tiles_m, unsigned int tiles_n, unsigned int* out);
+
+/* Human-readable text for a status code (static storage). */
+const char* b200gemm_strerror(int code);
+
+/* Library version as 10000*major + 100*minor + patch. */
+int b200gemm_version(void);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* B200GEMM_H_ */

@@ -1,0 +1,60 @@
+"""The C-ABI library loads without a GPU and exports every entry point that
+include/b200gemm.h declares; host-only logic (status strings, argument
+checks that precede any CUDA call, the tile schedule) works on the CPU."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from b200_gemm_b200 import _lib
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def _declared_symbols():
+    names = set()
+    for hdr in (ROOT / "include").glob("*.h"):
+        text = hdr.read_text()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        names |= set(re.findall(r"\b(b200gemm_\w+)\s*\(", text))
+    return names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    declared = _declared_symbols()
+    assert declared, "no declarations found"
+    assert declared == set(_lib.SIGNATURES), declared ^ set(_lib.SIGNATURES)
+    for name in declared:
+        assert hasattr(lib, name), name
+
+
+def test_strerror_and_version():
+    for code in range(7):
+        assert _lib.strerror(code)
+    assert "unknown" in _lib.strerror(99)
+    assert _lib.load().b200gemm_version() >= 10000
+
+
+def test_null_handle_is_rejected_without_cuda():
+    lib = _lib.load()
+    assert lib.b200gemm_bf16_nt(None, 1, 1, 8, None, None, None, 8, None) == _lib.ERR_INVALID_ARG
+    assert lib.b200gemm_set_timeout_ns(None, 1) == _lib.ERR_INVALID_ARG
+    assert lib.b200gemm_last_device_status(None, None) == _lib.ERR_INVALID_ARG
+    assert lib.b200gemm_selftest_watchdog(None, 1, None) == _lib.ERR_INVALID_ARG
+    assert lib.b200gemm_create(None, 0) == _lib.ERR_INVALID_ARG
+    lib.b200gemm_destroy(None)
+
+
+def test_create_without_gpu_reports_no_device():
+    try:
+        import torch
+
+        if torch.cuda.is_available():
+            pytest.skip("a GPU is present")
+    except ImportError:
+        pass
+    h = ctypes.c_void_p()
+    assert _lib.load().b200gemm_create(ctypes.byref(h), 0) == _lib.ERR_NO_DEVICE
+    assert not h.value

@@ -1,0 +1,115 @@
+"""CPU checks of the oracle itself: bf16 rounding, known-answer GEMMs with
+exact integer arithmetic, fp32 CPU baseline vs fp64 reference, sampling."""
+import numpy as np
+import pytest
+
+from b200_gemm_b200 import data
+
+
+def test_bf16_round_to_nearest_even(oracle_mod):
+    o = oracle_mod
+    # 1 + 2^-8 is exactly halfway between bf16 1.0 and 1.0078125 -> even (1.0)
+    # 1 + 3*2^-8 is halfway between 1.0078125 and 1.015625 -> even (1.015625)
+    x = np.array([1.0, 1.0 + 2 ** -8, 1.0 + 3 * 2 ** -8, 1.0 + 2 ** -8 + 2 ** -20, -2.5,
+                  np.inf, -np.inf, 0.0, -0.0, 3.4e38, 1e-40], dtype=np.float32)
+    bits = o.f32_to_bf16(x)
+    back = o.bf16_to_f32(bits)
+    assert back[0] == 1.0
+    assert back[1] == 1.0
+    assert back[2] == 1.015625
+    assert back[3] == 1.0078125
+    assert back[4] == -2.5
+    assert np.isposinf(back[5]) and np.isneginf(back[6])
+    assert bits[7] == 0x0000 and bits[8] == 0x8000
+    assert np.isposinf(back[9])  # 3.4e38 is past the bf16 rounding midpoint above its max (3.3895e38)
+    nan_bits = o.f32_to_bf16(np.array([np.nan], dtype=np.float32))
+    assert np.isnan(o.bf16_to_f32(nan_bits))[0]
+    # numpy restatement used by the data generator agrees on random values
+    r = np.random.Generator(np.random.PCG64(1)).standard_normal(100000, dtype=np.float32) * 100
+    assert np.array_equal(o.f32_to_bf16(r), data.f32_to_bf16_bits(r))
+
+
+def _exact_int_case(M, N, K, lo, hi, seed):
+    rng = np.random.Generator(np.random.PCG64(seed))
+    a = rng.integers(lo, hi + 1, size=(M, K)).astype(np.int64)
+    b = rng.integers(lo, hi + 1, size=(N, K)).astype(np.int64)
+    exact = a @ b.T
+    return a, b, exact
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 1, 8), (7, 5, 64), (64, 48, 40), (130, 260, 72)])
+def test_known_answer_small_integers(oracle_mod, M, N, K):
+    """Entries in [-2, 2] with K <= 72: every partial sum is an integer of
+    magnitude <= 288 < 2^24 and the result is a bf16-exact integer only when
+    |C| <= 256, so compare in float64 and demand exact equality."""
+    o = oracle_mod
+    a, b, exact = _exact_int_case(M, N, K, -2, 2, seed=M * 1000 + N)
+    A = o.f32_to_bf16(a.astype(np.float32))
+    B = o.f32_to_bf16(b.astype(np.float32))
+    ref = o.gemm_f64(A, B)
+    assert np.array_equal(ref, exact.astype(np.float64))
+    bits = o.gemm_bf16(A, B)
+    expect = o.f32_to_bf16(exact.astype(np.float32))
+    assert np.array_equal(bits, expect)
+
+
+def test_known_answer_identity_and_permutation(oracle_mod):
+    o = oracle_mod
+    rng = np.random.Generator(np.random.PCG64(7))
+    n = 96
+    A = o.f32_to_bf16(rng.standard_normal((80, n), dtype=np.float32))
+    eye = o.f32_to_bf16(np.eye(n, dtype=np.float32))
+    assert np.array_equal(o.gemm_bf16(A, eye), A)  # A . I^T = A
+    perm = rng.permutation(n)
+    P = o.f32_to_bf16(np.eye(n, dtype=np.float32)[perm])
+    assert np.array_equal(o.gemm_bf16(A, P), A[:, perm])
+
+
+def test_f32_cpu_baseline_within_tolerance(oracle_mod):
+    o = oracle_mod
+    A, B = data.host_operands(67, 93, 520, "normal", seed=3)
+    ref = o.gemm_f64(A, B)
+    got, used = o.gemm_f32_cpu(A, B, threads=3)
+    assert used >= 1
+    assert o.within_tolerance(o.bf16_to_f32(got), ref).all()
+    # row band only
+    part, _ = o.gemm_f32_cpu(A, B, row_begin=10, row_end=33, threads=2)
+    assert np.array_equal(part, got[10:33])
+
+
+def test_sampled_matches_full(oracle_mod):
+    o = oracle_mod
+    A, B = data.host_operands(50, 40, 136, "uniform", seed=5)
+    full = o.gemm_f64(A, B)
+    rows = np.array([0, 49, 13, 7], dtype=np.int32)
+    cols = np.array([39, 0, 22, 7], dtype=np.int32)
+    assert np.array_equal(o.gemm_sampled(A, B, rows, cols), full[rows, cols])
+
+
+def test_tolerance_rule(oracle_mod):
+    o = oracle_mod
+    ref = np.array([0.0, 100.0, -100.0])
+    ok = o.within_tolerance(np.array([2 ** -7, 100.0 + 101 * 2 ** -7, -100.5]), ref)
+    assert ok.all()
+    bad = o.within_tolerance(np.array([0.01, 100.0 + 2.0, -99.0]), ref)
+    assert not bad.any()
+    # the planted mistake is caught: flip one oracle output by a few ulps
+    A, B = data.host_operands(16, 16, 64, "normal", seed=11)
+    ref = o.gemm_f64(A, B)
+    wrong = ref.copy()
+    wrong[3, 4] += 0.5 + abs(ref[3, 4]) * 0.05
+    assert not o.within_tolerance(wrong, ref).all()
+
+
+@pytest.mark.parametrize("dist", data.DISTS)
+def test_generators_are_seeded(dist):
+    a1, b1 = data.host_operands(8, 9, 16, dist, seed=42)
+    a2, b2 = data.host_operands(8, 9, 16, dist, seed=42)
+    a3, _ = data.host_operands(8, 9, 16, dist, seed=43)
+    assert np.array_equal(a1, a2) and np.array_equal(b1, b2)
+    assert not np.array_equal(a1, a3)
+    bf = data.bf16_bits_to_f32(b1)
+    if dist == "mlp":
+        assert np.abs(bf).max() < 0.2
+    if dist == "uniform":
+        assert np.abs(bf).max() <= 1.0
