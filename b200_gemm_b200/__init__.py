@@ -98,6 +98,12 @@ class Gemm:
         _lib.check(rc, "b200gemm_bf16_nt")
         return out
 
+    def device_info(self) -> dict:
+        sm, cl = ctypes.c_int(), ctypes.c_int()
+        _lib.check(self._lib.b200gemm_device_info(self._h, ctypes.byref(sm), ctypes.byref(cl)),
+                   "b200gemm_device_info")
+        return {"sm_count": sm.value, "max_clusters": cl.value}
+
     def last_device_status(self):
         detail = (ctypes.c_uint * 4)()
         rc = self._lib.b200gemm_last_device_status(self._h, detail)

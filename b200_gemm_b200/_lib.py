@@ -31,6 +31,7 @@ SIGNATURES = {
     "b200gemm_set_timeout_ns": (_c_int, [_vp, _c_ull]),
     "b200gemm_selftest_watchdog": (_c_int, [_vp, _c_ull, _vp]),
     "b200gemm_run_kernel": (_c_int, [_c_int, _c_int, _c_int, _vp, _vp, _vp, ctypes.POINTER(_c_int)]),
+    "b200gemm_device_info": (_c_int, [_vp, ctypes.POINTER(_c_int), ctypes.POINTER(_c_int)]),
     "b200gemm_schedule_host": (_c_int, [_c_uint, _c_uint, ctypes.POINTER(_c_uint)]),
     "b200gemm_strerror": (ctypes.c_char_p, [_c_int]),
     "b200gemm_version": (_c_int, []),

@@ -327,6 +327,8 @@ extern "C" int b200gemm_bf16_nt(b200gemm_t h, int M, int N, int K, const void* A
   p.tiles = sched;
   p.status = h->status_dev;
   p.timeout_ns = timeout_ns;
+  p.C = static_cast<uint16_t*>(C);
+  p.ldc = ldc;
 
   const int clusters = p.num_tiles < h->max_clusters ? p.num_tiles : h->max_clusters;
   cudaLaunchConfig_t cfg = {};
@@ -360,6 +362,13 @@ extern "C" int b200gemm_selftest_watchdog(b200gemm_t h, unsigned long long timeo
   watchdog_selftest_kernel<<<2, 32, 0, static_cast<cudaStream_t>(stream_ptr)>>>(h->status_dev,
                                                                                timeout_ns);
   return cudaGetLastError() == cudaSuccess ? B200GEMM_OK : B200GEMM_ERR_CUDA;
+}
+
+extern "C" int b200gemm_device_info(b200gemm_t h, int* sm_count, int* max_clusters) {
+  if (h == nullptr) return B200GEMM_ERR_INVALID_ARG;
+  if (sm_count != nullptr) *sm_count = h->sm_count;
+  if (max_clusters != nullptr) *max_clusters = h->max_clusters;
+  return B200GEMM_OK;
 }
 
 extern "C" int b200gemm_schedule_host(unsigned int tiles_m, unsigned int tiles_n,

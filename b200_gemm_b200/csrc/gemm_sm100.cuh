@@ -16,6 +16,8 @@
 //     them out with per-warp TMA stores, double-buffered;
 //   * ragged M, N and K (K % 8 == 0) are handled by TMA bounds (zero fill on
 //     loads, clipping on stores) instead of requiring multiples of 256/64;
+//     the one chunk that ends inside a 16-byte group when N % 8 != 0 is
+//     stored element by element;
 //   * every wait is bounded (see ptx_sm100.cuh).
 //
 // Warp roles (192 threads per CTA, one CTA per SM, clusters of 2 CTAs):
@@ -62,6 +64,8 @@ struct GemmParams {
   const uint32_t* tiles;      // schedule: num_tiles packed (tm << 16 | tn) in curve order
   unsigned int* status;       // 4 status words (code, site, cta, tile); may be null
   unsigned long long timeout_ns;
+  uint16_t* C;                // C base (bf16 bits), for the ragged-N edge chunk
+  long long ldc;              // C row pitch in elements
 };
 
 template <int STAGES>
@@ -266,7 +270,22 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
         for (int i = 0; i < 16; ++i) pk[16 + i] = ptx::pack_bf16x2(v1[2 * i], v1[2 * i + 1]);
         const int col = col0 + c * kCBoxCols;
         const bool store = (row < p.M) && (col < p.N);  // warp-uniform
-        if (store) {
+        // TMA clips the innermost dimension in 16-byte units, so a chunk that
+        // ends inside a 16-byte group (N % 8 != 0) is written with plain,
+        // per-element predicated stores instead.
+        const bool ragged = ((p.N & 7) != 0) && (col + kCBoxCols > p.N);
+        if (store && ragged) {
+          const int r = row + static_cast<int>(lane);
+          if (r < p.M) {
+            uint16_t* dst = p.C + static_cast<long long>(r) * p.ldc + col;
+            const int ncols = p.N - col;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              if (2 * i < ncols) dst[2 * i] = static_cast<uint16_t>(pk[i] & 0xFFFFu);
+              if (2 * i + 1 < ncols) dst[2 * i + 1] = static_cast<uint16_t>(pk[i] >> 16);
+            }
+          }
+        } else if (store) {
           const uint32_t buf = cstage0 + cbuf * kCStageBytes;
           // The TMA store that last read this buffer (two stores ago) must be done reading.
           if (lane == 0) ptx::bulk_wait_group_read<1>();

@@ -357,6 +357,7 @@ def run_ours(args, w):
         extra["e2e"] = e2e
 
     del A, B, C
+    info = gemm.device_info()
     result = None
     if rank == 0:
         peaks, peak_kind = load_peaks()
@@ -375,6 +376,7 @@ def run_ours(args, w):
                               % ((M * K + Nl * K) * 2 / 1e6)) if (M * K + Nl * K) * 2 > L2_BYTES
                        else "operands fit in L2: NOT flushed"},
             "gpu_launches": args.steps,
+            "launch": dict(info, threads_per_cta=192, cluster=2),
             "roofline": {"bound": "tensor", "achieved": kernel_tflops, "peak": peak, "unit": "TFLOP/s",
                          "frac": kernel_tflops / peak, "peak_kind": f"{peak_kind} bf16_tflops (burst)",
                          "traffic": traffic,

@@ -76,6 +76,12 @@ int b200gemm_selftest_watchdog(b200gemm_t handle, unsigned long long timeout_ns,
  * matmul_b200.cu:35) is accepted and ignored. */
 int b200gemm_run_kernel(int M, int N, int K, const void* A, const void* B, void* C, int* DB);
 
+/* Launch geometry chosen for the handle's device: SM count and the number of
+ * 2-CTA clusters of the GEMM kernel that fit on the device at once (the
+ * persistent grid size).  Either pointer may be null.  The reference fixes
+ * both at compile time (NUM_SM = 148, matmul_1.cuh:19). */
+int b200gemm_device_info(b200gemm_t handle, int* sm_count, int* max_clusters);
+
 /* Host computation of the persistent tile schedule the kernel follows for a
  * tiles_m x tiles_n grid of 256 x 256 output tiles: out[0 .. tiles_m*tiles_n)
  * receives (tile_m << 16 | tile_n) in Hilbert-curve order; entry j runs on

@@ -27,9 +27,11 @@ def _host_bits(t):
 def _run(h, A_bits, B_bits, ldc=None, poison=True):
     M, K = A_bits.shape
     N = B_bits.shape[0]
-    ldc = N if ldc is None else ldc
+    full = ldc is not None  # caller wants the whole [M, ldc] buffer back
+    ldc = 8 * ((N + 7) // 8) if ldc is None else ldc  # row pitch must be a multiple of 16 bytes
     A, B = _dev(A_bits), _dev(B_bits)
-    C = torch.full((max(M, 1), ldc), 0, dtype=torch.int16, device="cuda")
+    guard = 64  # poisoned rows after the last row of C: must stay untouched
+    C = torch.full((M + guard, ldc), 0, dtype=torch.int16, device="cuda")
     if poison:
         C.fill_(NAN_BF16)
     C = C.view(torch.bfloat16)
@@ -38,7 +40,12 @@ def _run(h, A_bits, B_bits, ldc=None, poison=True):
     torch.cuda.synchronize()
     st, detail = h.last_device_status()
     assert st == _lib.OK, detail
-    return _host_bits(C)[:M]
+    allc = _host_bits(C)
+    fill = NAN_BF16 if poison else 0
+    assert np.all(allc[M:] == fill), "write past row M"
+    out = allc[:M]
+    assert np.all(out[:, N:] == fill), "write outside the N columns"
+    return out if full else out[:, :N]
 
 
 SHAPES = [
@@ -51,6 +58,8 @@ SHAPES = [
     (257, 257, 136),
     (129, 1000, 520),
     (1000, 40, 1032),
+    (300, 77, 64),      # N % 8 != 0 inside the first tile
+    (40, 1003, 200),    # N % 8 != 0 in the last tile column
     (2560, 2560, 128),  # 100 tiles: more tiles than clusters
     (256, 256, 4096),   # long K: the smem ring wraps many times
 ]
@@ -109,6 +118,12 @@ def test_k_zero_writes_zeros(gpu_handle):
     assert rc == _lib.OK
     torch.cuda.synchronize()
     assert np.all(_host_bits(C) == 0)
+
+
+def test_device_info(gpu_handle):
+    info = gpu_handle.device_info()
+    assert info["sm_count"] >= 100
+    assert 1 <= info["max_clusters"] <= info["sm_count"] // 2
 
 
 def test_argument_errors(gpu_handle):
