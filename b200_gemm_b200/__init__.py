@@ -98,6 +98,18 @@ class Gemm:
         _lib.check(rc, "b200gemm_bf16_nt")
         return out
 
+    def set_tile_width(self, width: int) -> None:
+        """0 = choose per call (default), 256 or 512 output columns per tile."""
+        _lib.check(self._lib.b200gemm_set_tile_width(self._h, int(width)), "b200gemm_set_tile_width")
+
+    def tile_width_for(self, M: int, N: int, K: int) -> int:
+        return int(self._lib.b200gemm_tile_width_for(self._h, M, N, K))
+
+    def set_schedule(self, order: int, band: int = 8) -> None:
+        """Tile start order: _lib.ORDER_HILBERT or _lib.ORDER_BANDS (band = tile-rows)."""
+        _lib.check(self._lib.b200gemm_set_schedule(self._h, int(order), int(band)),
+                   "b200gemm_set_schedule")
+
     def device_info(self) -> dict:
         sm, cl = ctypes.c_int(), ctypes.c_int()
         _lib.check(self._lib.b200gemm_device_info(self._h, ctypes.byref(sm), ctypes.byref(cl)),
@@ -154,9 +166,10 @@ def run_kernel(kernel_num: int, M: int, N: int, K: int, A, B, C) -> None:
         raise ValueError(f"kernel {kernel_num}: 0 = cuBLASLt, 2 = b200gemm")
 
 
-def schedule(tiles_m: int, tiles_n: int):
+def schedule(tiles_m: int, tiles_n: int, order: int = _lib.ORDER_HILBERT, band: int = 8):
     """Host copy of the kernel's tile order (list of (tile_m, tile_n))."""
     n = tiles_m * tiles_n
     buf = (ctypes.c_uint * n)()
-    _lib.check(_lib.load().b200gemm_schedule_host(tiles_m, tiles_n, buf), "b200gemm_schedule_host")
+    _lib.check(_lib.load().b200gemm_schedule_host(tiles_m, tiles_n, order, band, buf),
+               "b200gemm_schedule_host")
     return [(v >> 16, v & 0xFFFF) for v in buf]

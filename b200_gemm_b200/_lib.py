@@ -20,6 +20,9 @@ ERR_DEVICE_TIMEOUT = 4
 ERR_NO_DEVICE = 5
 ERR_TOO_LARGE = 6
 
+ORDER_HILBERT = 0
+ORDER_BANDS = 1
+
 _c_int, _c_uint, _c_ull, _vp = ctypes.c_int, ctypes.c_uint, ctypes.c_ulonglong, ctypes.c_void_p
 
 # name -> (restype, argtypes); one line per declaration in include/b200gemm.h
@@ -32,7 +35,10 @@ SIGNATURES = {
     "b200gemm_selftest_watchdog": (_c_int, [_vp, _c_ull, _vp]),
     "b200gemm_run_kernel": (_c_int, [_c_int, _c_int, _c_int, _vp, _vp, _vp, ctypes.POINTER(_c_int)]),
     "b200gemm_device_info": (_c_int, [_vp, ctypes.POINTER(_c_int), ctypes.POINTER(_c_int)]),
-    "b200gemm_schedule_host": (_c_int, [_c_uint, _c_uint, ctypes.POINTER(_c_uint)]),
+    "b200gemm_set_tile_width": (_c_int, [_vp, _c_int]),
+    "b200gemm_tile_width_for": (_c_int, [_vp, _c_int, _c_int, _c_int]),
+    "b200gemm_set_schedule": (_c_int, [_vp, _c_int, _c_int]),
+    "b200gemm_schedule_host": (_c_int, [_c_uint, _c_uint, _c_int, _c_int, ctypes.POINTER(_c_uint)]),
     "b200gemm_strerror": (ctypes.c_char_p, [_c_int]),
     "b200gemm_version": (_c_int, []),
 }

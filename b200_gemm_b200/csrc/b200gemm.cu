@@ -17,13 +17,25 @@
 
 namespace b200gemm {
 
-constexpr int kStages = 6;
+// Pipeline depth of each kernel instance (build-time tuning knobs).
+#ifndef B200GEMM_STAGES_N256
+#define B200GEMM_STAGES_N256 6
+#endif
+#ifndef B200GEMM_STAGES_N512
+#define B200GEMM_STAGES_N512 4
+#endif
+#ifndef B200GEMM_DEFAULT_ORDER
+#define B200GEMM_DEFAULT_ORDER 0
+#endif
+#ifndef B200GEMM_DEFAULT_BAND
+#define B200GEMM_DEFAULT_BAND 8
+#endif
+using CfgN256 = GemmCfg<B200GEMM_STAGES_N256, 1>;  // 256 x 256 tiles, overlapped epilogue
+using CfgN512 = GemmCfg<B200GEMM_STAGES_N512, 2>;  // 256 x 512 tiles, shared A stage
 constexpr int kVersion = 10000;  // 1.0.0
 constexpr int kMapCacheSize = 8;
 constexpr size_t kScheduleCacheSize = 16;
 constexpr unsigned long long kDefaultTimeoutNs = 2000000000ull;
-
-using Layout = SmemLayout<kStages>;
 
 // Restores the caller's current device on scope exit.
 class DeviceGuard {
@@ -88,15 +100,62 @@ struct MapEntry {
 
 struct ScheduleEntry {
   uint32_t tiles_m = 0, tiles_n = 0;
+  int order = 0;
+  uint32_t band = 0;
   uint32_t* dev = nullptr;
   uint64_t last_use = 0;
 };
 
-int set_gemm_attributes() {
-  const cudaError_t e = cudaFuncSetAttribute(gemm_bf16_nt_sm100<kStages>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             Layout::kBytes);
-  return e == cudaSuccess ? B200GEMM_OK : B200GEMM_ERR_CUDA;
+// Opt the kernel instance into its shared memory size and return how many
+// of its 2-CTA clusters fit on the device at once (0 on failure).
+template <class Cfg>
+int prepare_kernel(int sm_count) {
+  if (cudaFuncSetAttribute(gemm_bf16_nt_sm100<Cfg>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           Cfg::kSmemBytes) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(static_cast<unsigned>(sm_count & ~1), 1, 1);
+  cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, gemm_bf16_nt_sm100<Cfg>, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return clusters;
+}
+
+template <class Cfg>
+cudaError_t launch_gemm(int clusters, cudaStream_t stream, const CUtensorMap& ma,
+                        const CUtensorMap& mb, const CUtensorMap& mc, const GemmParams& p) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * clusters), 1, 1);
+  cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.stream = stream;
+  return cudaLaunchKernelEx(&cfg, gemm_bf16_nt_sm100<Cfg>, ma, mb, mc, p);
+}
+
+// Relative cost of a GEMM with tiles of `nb` 256-column blocks: waves of
+// persistent clusters times the time of one tile, in units of one 64-deep K
+// block of a 256 x 256 tile at full tensor rate.  The efficiencies are the
+// measured tensor-pipe activity of each instance on large problems; the
+// 512-wide tile also pays its non-overlapped epilogue (about 4 K blocks).
+double tile_plan_cost(int nb, uint32_t tiles_m, int N, int num_kb, int clusters) {
+  const uint64_t tiles_n = (static_cast<uint64_t>(N) + 256u * nb - 1) / (256u * nb);
+  const uint64_t tiles = tiles_m * tiles_n;
+  const uint64_t waves = (tiles + clusters - 1) / clusters;
+  const double tile_time = nb == 1 ? num_kb / 0.85 : (2.0 * num_kb + 4.0) / 0.93;
+  return static_cast<double>(waves) * tile_time;
 }
 
 }  // namespace b200gemm
@@ -106,9 +165,14 @@ using namespace b200gemm;
 struct b200gemm_handle {
   int device = 0;
   int sm_count = 0;
-  int max_clusters = 0;  // co-resident 2-CTA clusters of the GEMM kernel
+  int max_clusters = 0;       // co-resident 2-CTA clusters (the smaller of the two instances)
+  int clusters_n256 = 0;      // co-resident clusters of the 256-wide instance
+  int clusters_n512 = 0;      // co-resident clusters of the 512-wide instance
+  int tile_width = 0;         // 0 = choose per call, else 256 or 512
   unsigned int* status_dev = nullptr;
   unsigned long long timeout_ns = kDefaultTimeoutNs;
+  int order = B200GEMM_DEFAULT_ORDER;      // tile order (schedule.cuh)
+  uint32_t band = B200GEMM_DEFAULT_BAND;   // tile-rows per band for the band order
   std::mutex mu;
   uint64_t tick = 0;
   MapEntry maps[kMapCacheSize];
@@ -144,31 +208,17 @@ extern "C" int b200gemm_create(b200gemm_t* out, int device) {
   if (prop.major != 10 || prop.minor != 0) return B200GEMM_ERR_NO_DEVICE;
   DeviceGuard guard(device);
   if (!guard.ok()) return B200GEMM_ERR_CUDA;
-  if (set_gemm_attributes() != B200GEMM_OK) return B200GEMM_ERR_CUDA;
   if (tensor_map_encoder() == nullptr) return B200GEMM_ERR_CUDA;
-
-  cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.gridDim = dim3(prop.multiProcessorCount & ~1, 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = Layout::kBytes;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  int clusters = 0;
-  if (cudaOccupancyMaxActiveClusters(&clusters, gemm_bf16_nt_sm100<kStages>, &cfg) != cudaSuccess ||
-      clusters <= 0) {
-    cudaGetLastError();
-    return B200GEMM_ERR_CUDA;
-  }
+  const int c256 = prepare_kernel<CfgN256>(prop.multiProcessorCount);
+  const int c512 = prepare_kernel<CfgN512>(prop.multiProcessorCount);
+  if (c256 <= 0 || c512 <= 0) return B200GEMM_ERR_CUDA;
 
   auto* h = new b200gemm_handle();
   h->device = device;
   h->sm_count = prop.multiProcessorCount;
-  h->max_clusters = clusters;
+  h->clusters_n256 = c256;
+  h->clusters_n512 = c512;
+  h->max_clusters = c256 < c512 ? c256 : c512;
   if (cudaMalloc(&h->status_dev, 4 * sizeof(unsigned int)) != cudaSuccess ||
       cudaMemset(h->status_dev, 0, 4 * sizeof(unsigned int)) != cudaSuccess) {
     cudaFree(h->status_dev);
@@ -204,7 +254,7 @@ namespace {
 int schedule_for(b200gemm_t h, uint32_t tiles_m, uint32_t tiles_n, cudaStream_t stream,
                  const uint32_t** out) {
   for (auto& s : h->schedules) {
-    if (s.tiles_m == tiles_m && s.tiles_n == tiles_n) {
+    if (s.tiles_m == tiles_m && s.tiles_n == tiles_n && s.order == h->order && s.band == h->band) {
       s.last_use = ++h->tick;
       *out = s.dev;
       return B200GEMM_OK;
@@ -220,9 +270,11 @@ int schedule_for(b200gemm_t h, uint32_t tiles_m, uint32_t tiles_n, cudaStream_t 
   ScheduleEntry e;
   e.tiles_m = tiles_m;
   e.tiles_n = tiles_n;
+  e.order = h->order;
+  e.band = h->band;
   const size_t bytes = static_cast<size_t>(tiles_m) * tiles_n * sizeof(uint32_t);
   if (cudaMalloc(&e.dev, bytes) != cudaSuccess) return B200GEMM_ERR_CUDA;
-  build_hilbert_schedule_kernel<<<1, 1024, 0, stream>>>(tiles_m, tiles_n, e.dev);
+  build_schedule_kernel<<<1, 1024, 0, stream>>>(tiles_m, tiles_n, e.order, e.band, e.dev);
   // Wait once so the table is valid for launches on any stream.
   if (cudaGetLastError() != cudaSuccess || cudaStreamSynchronize(stream) != cudaSuccess) {
     cudaFree(e.dev);
@@ -282,6 +334,20 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 }  // namespace
 
+namespace {
+
+// Tile width (256 or 512 columns) a call on this handle will use.
+int choose_tile_width(const b200gemm_handle* h, int M, int N, int K) {
+  if (h->tile_width != 0) return h->tile_width;
+  const uint32_t tiles_m = static_cast<uint32_t>((M + kTileM - 1) / kTileM);
+  const int num_kb = (K + kBlockK - 1) / kBlockK;
+  const double c256 = tile_plan_cost(1, tiles_m, N, num_kb, h->clusters_n256);
+  const double c512 = tile_plan_cost(2, tiles_m, N, num_kb, h->clusters_n512);
+  return c512 < c256 ? 512 : 256;
+}
+
+}  // namespace
+
 extern "C" int b200gemm_bf16_nt(b200gemm_t h, int M, int N, int K, const void* A, const void* B,
                                 void* C, int ldc, void* stream_ptr) {
   if (h == nullptr || M < 0 || N < 0 || K < 0) return B200GEMM_ERR_INVALID_ARG;
@@ -290,11 +356,8 @@ extern "C" int b200gemm_bf16_nt(b200gemm_t h, int M, int N, int K, const void* A
   if (ldc < N || (ldc % 8) != 0 || (K % 8) != 0) return B200GEMM_ERR_UNSUPPORTED;
   if (!aligned16(C) || (K > 0 && (!aligned16(A) || !aligned16(B)))) return B200GEMM_ERR_UNSUPPORTED;
   const uint32_t tiles_m = static_cast<uint32_t>((M + kTileM - 1) / kTileM);
-  const uint32_t tiles_n = static_cast<uint32_t>((N + kTileN - 1) / kTileN);
-  if (tiles_m > 0xFFFFu || tiles_n > 0xFFFFu ||
-      static_cast<uint64_t>(tiles_m) * tiles_n > 0x7FFFFFFFull) {
+  if (tiles_m > 0xFFFFu || static_cast<uint32_t>((N + kBlockN - 1) / kBlockN) > 0xFFFFu)
     return B200GEMM_ERR_TOO_LARGE;
-  }
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
   DeviceGuard guard(h->device);
   if (!guard.ok()) return B200GEMM_ERR_CUDA;
@@ -309,8 +372,12 @@ extern "C" int b200gemm_bf16_nt(b200gemm_t h, int M, int N, int K, const void* A
   CUtensorMap ma, mb, mc;
   const uint32_t* sched = nullptr;
   unsigned long long timeout_ns;
+  int width;
+  uint32_t tiles_n;
   {
     std::lock_guard<std::mutex> lock(h->mu);
+    width = choose_tile_width(h, M, N, K);
+    tiles_n = static_cast<uint32_t>((N + width - 1) / width);
     int rc = schedule_for(h, tiles_m, tiles_n, stream, &sched);
     if (rc != B200GEMM_OK) return rc;
     rc = maps_for(h, M, N, K, A, B, C, ldc, &ma, &mb, &mc);
@@ -330,14 +397,28 @@ extern "C" int b200gemm_bf16_nt(b200gemm_t h, int M, int N, int K, const void* A
   p.C = static_cast<uint16_t*>(C);
   p.ldc = ldc;
 
-  const int clusters = p.num_tiles < h->max_clusters ? p.num_tiles : h->max_clusters;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(2 * clusters), 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = Layout::kBytes;
-  cfg.stream = stream;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_bf16_nt_sm100<kStages>, ma, mb, mc, p);
+  cudaError_t e;
+  if (width == 512) {
+    const int clusters = p.num_tiles < h->clusters_n512 ? p.num_tiles : h->clusters_n512;
+    e = launch_gemm<CfgN512>(clusters, stream, ma, mb, mc, p);
+  } else {
+    const int clusters = p.num_tiles < h->clusters_n256 ? p.num_tiles : h->clusters_n256;
+    e = launch_gemm<CfgN256>(clusters, stream, ma, mb, mc, p);
+  }
   return e == cudaSuccess ? B200GEMM_OK : B200GEMM_ERR_CUDA;
+}
+
+extern "C" int b200gemm_set_tile_width(b200gemm_t h, int width) {
+  if (h == nullptr || (width != 0 && width != 256 && width != 512)) return B200GEMM_ERR_INVALID_ARG;
+  std::lock_guard<std::mutex> lock(h->mu);
+  h->tile_width = width;
+  return B200GEMM_OK;
+}
+
+extern "C" int b200gemm_tile_width_for(b200gemm_t h, int M, int N, int K) {
+  if (h == nullptr || M <= 0 || N <= 0 || K < 0) return 0;
+  std::lock_guard<std::mutex> lock(h->mu);
+  return choose_tile_width(h, M, N, K);
 }
 
 extern "C" int b200gemm_last_device_status(b200gemm_t h, unsigned int* detail) {
@@ -371,18 +452,21 @@ extern "C" int b200gemm_device_info(b200gemm_t h, int* sm_count, int* max_cluste
   return B200GEMM_OK;
 }
 
-extern "C" int b200gemm_schedule_host(unsigned int tiles_m, unsigned int tiles_n,
-                                      unsigned int* out) {
-  if (out == nullptr || tiles_m == 0 || tiles_n == 0 || tiles_m > 0xFFFFu || tiles_n > 0xFFFFu)
+extern "C" int b200gemm_set_schedule(b200gemm_t h, int order, int band) {
+  if (h == nullptr || (order != kOrderHilbert && order != kOrderBands) || band < 1 || band > 0xFFFF)
     return B200GEMM_ERR_INVALID_ARG;
-  const uint32_t side = hilbert_side(tiles_m, tiles_n);
-  const uint64_t cells = static_cast<uint64_t>(side) * side;
-  uint64_t w = 0;
-  for (uint64_t d = 0; d < cells; ++d) {
-    uint32_t x, y;
-    hilbert_cell(side, static_cast<uint32_t>(d), x, y);
-    if (x < tiles_m && y < tiles_n) out[w++] = pack_tile(x, y);
-  }
+  std::lock_guard<std::mutex> lock(h->mu);
+  h->order = order;
+  h->band = static_cast<uint32_t>(band);
+  return B200GEMM_OK;
+}
+
+extern "C" int b200gemm_schedule_host(unsigned int tiles_m, unsigned int tiles_n, int order,
+                                      int band, unsigned int* out) {
+  if (out == nullptr || tiles_m == 0 || tiles_n == 0 || tiles_m > 0xFFFFu || tiles_n > 0xFFFFu ||
+      (order != kOrderHilbert && order != kOrderBands) || band < 1 || band > 0xFFFF)
+    return B200GEMM_ERR_INVALID_ARG;
+  build_schedule_host(tiles_m, tiles_n, order, static_cast<uint32_t>(band), out);
   return B200GEMM_OK;
 }
 

@@ -31,21 +31,27 @@
 
 #include "ptx_sm100.cuh"
 
+// L2 eviction priority of the operand loads (0 normal, 1 evict_last,
+// 2 evict_first); build-time tuning knobs.
+#ifndef B200GEMM_L2_POLICY_A
+#define B200GEMM_L2_POLICY_A 0
+#endif
+#ifndef B200GEMM_L2_POLICY_B
+#define B200GEMM_L2_POLICY_B 0
+#endif
+
 namespace b200gemm {
 
-constexpr int kTileM = 256;   // rows of C per CTA pair (128 per CTA)
-constexpr int kTileN = 256;   // columns of C per CTA pair (= MMA N)
-constexpr int kBlockK = 64;   // K per pipeline stage: one 128-byte swizzle row of bf16
-constexpr int kMmaK = 16;     // K per tcgen05.mma (kind::f16)
-constexpr int kThreads = 192;
-constexpr int kAccCols = 256;     // fp32 TMEM columns per accumulator
-constexpr int kTmemCols = 512;    // two accumulators
-constexpr int kStageBytesA = 128 * kBlockK * 2;  // per CTA per stage
-constexpr int kStageBytesB = 128 * kBlockK * 2;  // per CTA per stage (half of the pair's 256 rows)
+constexpr int kTileM = 256;       // rows of C per CTA pair (128 per CTA)
+constexpr int kBlockN = 256;      // columns per tcgen05.mma (N of one instruction)
+constexpr int kBlockK = 64;       // K per pipeline stage: one 128-byte swizzle row of bf16
+constexpr int kMmaK = 16;         // K per tcgen05.mma (kind::f16)
+constexpr int kTmemCols = 512;    // the whole TMEM of the SM
+constexpr int kStageBytesA = 128 * kBlockK * 2;       // A rows of one CTA, one stage
+constexpr int kBlockBytesB = 128 * kBlockK * 2;       // B rows of one CTA for one N block
 constexpr int kCBoxCols = 64;     // one 128-byte row of bf16
 constexpr int kCBoxRows = 32;     // one warp's TMEM lane quarter
 constexpr int kCStageBytes = kCBoxCols * kCBoxRows * 2;
-constexpr int kEpilogueWarps = 4;
 
 // Watchdog sites (reported in status word 1).
 enum : unsigned int {
@@ -60,29 +66,46 @@ enum : unsigned int {
 struct GemmParams {
   int M, N, K;
   int num_kb;                 // ceil(K / kBlockK)
-  int num_tiles;              // ceil(M/256) * ceil(N/256)
-  const uint32_t* tiles;      // schedule: num_tiles packed (tm << 16 | tn) in curve order
+  int num_tiles;              // ceil(M / 256) * ceil(N / tile width)
+  const uint32_t* tiles;      // schedule: num_tiles packed (tm << 16 | tn) in start order
   unsigned int* status;       // 4 status words (code, site, cta, tile); may be null
   unsigned long long timeout_ns;
   uint16_t* C;                // C base (bf16 bits), for the ragged-N edge chunk
   long long ldc;              // C row pitch in elements
 };
 
-template <int STAGES>
-struct SmemLayout {
+// Compile-time shape of one kernel instance.
+//   NB = 1: a pair computes 256 x 256 tiles; TMEM holds two accumulators, so
+//           the MMA of tile i+1 overlaps the epilogue of tile i.
+//   NB = 2: a pair computes 256 x 512 tiles as two N = 256 MMAs per K step
+//           that share the A stage: 25% fewer operand bytes into each SM per
+//           flop; the single 512-column accumulator is drained by 8 warps.
+template <int STAGES, int NB>
+struct GemmCfg {
+  static_assert(NB == 1 || NB == 2, "tile width is 256 or 512 columns");
+  static constexpr int kStages = STAGES;
+  static constexpr int kNB = NB;
+  static constexpr int kTileN = kBlockN * NB;
+  static constexpr int kAccBufs = kTmemCols / kTileN;
+  static constexpr int kEpiWarps = 4 * NB;
+  static constexpr int kThreads = 64 + 32 * kEpiWarps;
+  static constexpr int kCBufs = (NB == 1) ? 2 : 1;   // staging buffers per epilogue warp
+  static constexpr int kStageBytesB = kBlockBytesB * NB;
+  static constexpr uint32_t kTxBytes = 2 * (kStageBytesA + kStageBytesB);  // both CTAs
+  // shared memory layout (offsets from a 1024-byte aligned base)
   static constexpr int kA = 0;
   static constexpr int kB = kA + STAGES * kStageBytesA;
   static constexpr int kC = kB + STAGES * kStageBytesB;
-  static constexpr int kFull = kC + kEpilogueWarps * 2 * kCStageBytes;
+  static constexpr int kFull = kC + kEpiWarps * kCBufs * kCStageBytes;
   static constexpr int kEmpty = kFull + 8 * STAGES;
   static constexpr int kTFull = kEmpty + 8 * STAGES;
-  static constexpr int kTEmpty = kTFull + 16;
-  static constexpr int kDrain = kTEmpty + 16;
+  static constexpr int kTEmpty = kTFull + 8 * kAccBufs;
+  static constexpr int kDrain = kTEmpty + 8 * kAccBufs;
   static constexpr int kTmemSlot = kDrain + 8;
   static constexpr int kAbort = kTmemSlot + 4;
   static constexpr int kEnd = kAbort + 4;
-  static constexpr int kBytes = kEnd + 1024;  // slack to align the base to 1024 B
-  static_assert(kBytes <= 232448, "exceeds the 227 KB per-CTA shared memory limit");
+  static constexpr int kSmemBytes = kEnd + 1024;  // slack to align the base to 1024 B
+  static_assert(kSmemBytes <= 232448, "exceeds the 227 KB per-CTA shared memory limit");
 };
 
 // Instruction descriptor, kind::f16: D = f32, A = B = bf16, both K-major,
@@ -90,7 +113,7 @@ struct SmemLayout {
 constexpr uint32_t kIdescBf16 = (1u << 4)            // D format f32
                                 | (1u << 7)          // A format bf16
                                 | (1u << 10)         // B format bf16
-                                | ((kTileN >> 3) << 17) | ((kTileM >> 4) << 24);
+                                | ((kBlockN >> 3) << 17) | ((kTileM >> 4) << 24);
 
 // Shared-memory matrix descriptor fields above the start address for a
 // K-major operand in the 128-byte swizzle layout written by TMA: 8-row groups
@@ -102,12 +125,13 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
   return kSmemDescHi | uint64_t((addr & 0x3FFFFu) >> 4);
 }
 
-template <int STAGES>
-__global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
+template <class Cfg>
+__global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
     gemm_bf16_nt_sm100(const __grid_constant__ CUtensorMap map_a,
                        const __grid_constant__ CUtensorMap map_b,
                        const __grid_constant__ CUtensorMap map_c, const GemmParams p) {
-  using L = SmemLayout<STAGES>;
+  constexpr int STAGES = Cfg::kStages;
+  constexpr int NB = Cfg::kNB;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const uint32_t raw = ptx::smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -118,13 +142,13 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
   const uint32_t cluster = ptx::cluster_id_x();
   const uint32_t nclusters = ptx::num_clusters_x();
 
-  const uint32_t sA = base + L::kA, sB = base + L::kB, sC = base + L::kC;
-  const uint32_t full0 = base + L::kFull, empty0 = base + L::kEmpty;
-  const uint32_t tfull0 = base + L::kTFull, tempty0 = base + L::kTEmpty;
-  const uint32_t drain = base + L::kDrain, tmem_slot = base + L::kTmemSlot;
+  const uint32_t sA = base + Cfg::kA, sB = base + Cfg::kB, sC = base + Cfg::kC;
+  const uint32_t full0 = base + Cfg::kFull, empty0 = base + Cfg::kEmpty;
+  const uint32_t tfull0 = base + Cfg::kTFull, tempty0 = base + Cfg::kTEmpty;
+  const uint32_t drain = base + Cfg::kDrain, tmem_slot = base + Cfg::kTmemSlot;
 
   ptx::Watchdog wd;
-  wd.abort_flag = base + L::kAbort;
+  wd.abort_flag = base + Cfg::kAbort;
   wd.peer_abort_flag = ptx::mapa(wd.abort_flag, rank ^ 1u);
   wd.status = p.status;
   wd.timeout_ns = p.timeout_ns;
@@ -135,9 +159,9 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
       ptx::mbar_init(full0 + 8 * s, 1);   // leader's expect_tx arrival (+ bytes of both CTAs)
       ptx::mbar_init(empty0 + 8 * s, 1);  // one MMA commit
     }
-    for (int a = 0; a < 2; ++a) {
-      ptx::mbar_init(tfull0 + 8 * a, 1);                    // one MMA commit
-      ptx::mbar_init(tempty0 + 8 * a, 2 * kEpilogueWarps);  // every epilogue warp of the pair
+    for (int a = 0; a < Cfg::kAccBufs; ++a) {
+      ptx::mbar_init(tfull0 + 8 * a, 1);                     // one MMA commit
+      ptx::mbar_init(tempty0 + 8 * a, 2 * Cfg::kEpiWarps);   // every epilogue warp of the pair
     }
     ptx::mbar_init(drain, 1);
     ptx::fence_mbar_init_cluster();
@@ -161,7 +185,8 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      const uint64_t policy = ptx::policy_evict_normal();
+      const uint64_t policy_a = ptx::l2_policy(B200GEMM_L2_POLICY_A);
+      const uint64_t policy_b = ptx::l2_policy(B200GEMM_L2_POLICY_B);
       const uint32_t full_leader0 = ptx::mapa(full0, 0);
       uint32_t stage = 0, phase = 0;
       bool ok = true;
@@ -170,16 +195,21 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
         const uint32_t tile = next;
         if (t + nclusters < num_tiles) next = __ldg(p.tiles + t + nclusters);
         const int row_a = static_cast<int>(tile >> 16) * kTileM + static_cast<int>(rank) * 128;
-        const int row_b = static_cast<int>(tile & 0xFFFFu) * kTileN + static_cast<int>(rank) * 128;
+        const int row_b =
+            static_cast<int>(tile & 0xFFFFu) * Cfg::kTileN + static_cast<int>(rank) * 128;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!ptx::mbar_wait(empty0 + 8 * stage, phase ^ 1u, wd, kSiteProducer, t)) {
             ok = false;
             break;
           }
-          if (leader) ptx::mbar_arrive_expect_tx(full0 + 8 * stage, 2 * (kStageBytesA + kStageBytesB));
+          if (leader) ptx::mbar_arrive_expect_tx(full0 + 8 * stage, Cfg::kTxBytes);
           const uint32_t fb = full_leader0 + 8 * stage;
-          ptx::tma_load_2d_cg2(sA + stage * kStageBytesA, &map_a, fb, kb * kBlockK, row_a, policy);
-          ptx::tma_load_2d_cg2(sB + stage * kStageBytesB, &map_b, fb, kb * kBlockK, row_b, policy);
+          ptx::tma_load_2d_cg2(sA + stage * kStageBytesA, &map_a, fb, kb * kBlockK, row_a, policy_a);
+#pragma unroll
+          for (int h = 0; h < NB; ++h) {
+            ptx::tma_load_2d_cg2(sB + stage * Cfg::kStageBytesB + h * kBlockBytesB, &map_b, fb,
+                                 kb * kBlockK, row_b + h * kBlockN, policy_b);
+          }
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -198,7 +228,7 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
       for (uint32_t t = cluster; t < num_tiles && ok; t += nclusters) {
         if (!ptx::mbar_wait(tempty0 + 8 * acc, acc_phase ^ 1u, wd, kSiteMmaTmemEmpty, t)) break;
         ptx::tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * kAccCols;
+        const uint32_t d_tmem = tmem_base + acc * Cfg::kTileN;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!ptx::mbar_wait(full0 + 8 * stage, phase, wd, kSiteMmaFull, t)) {
             ok = false;
@@ -206,12 +236,17 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
           }
           ptx::tc_fence_after();
           const uint64_t a_desc = smem_desc(sA + stage * kStageBytesA);
-          const uint64_t b_desc = smem_desc(sB + stage * kStageBytesB);
+          const uint64_t b_desc = smem_desc(sB + stage * Cfg::kStageBytesB);
 #pragma unroll
           for (int k = 0; k < kBlockK / kMmaK; ++k) {
-            // +32 bytes per K step inside the 128-byte swizzle row.
-            ptx::mma_bf16_cg2(d_tmem, a_desc + 2 * k, b_desc + 2 * k, kIdescBf16,
-                              (kb > 0 || k > 0) ? 1u : 0u);
+#pragma unroll
+            for (int h = 0; h < NB; ++h) {
+              // +32 bytes per K step inside the 128-byte swizzle row; the
+              // second N block of B sits kBlockBytesB further on.
+              ptx::mma_bf16_cg2(d_tmem + h * kBlockN, a_desc + 2 * k,
+                                b_desc + (h * kBlockBytesB >> 4) + 2 * k, kIdescBf16,
+                                (kb > 0 || k > 0) ? 1u : 0u);
+            }
           }
           ptx::mma_commit_cg2(own_empty0 + 8 * stage);
           ptx::mma_commit_cg2(peer_empty0 + 8 * stage);
@@ -223,8 +258,10 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
         if (!ok) break;
         ptx::mma_commit_cg2(own_tfull0 + 8 * acc);
         ptx::mma_commit_cg2(peer_tfull0 + 8 * acc);
-        acc ^= 1u;
-        if (acc == 0) acc_phase ^= 1u;
+        if (++acc == Cfg::kAccBufs) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
       }
       // Every MMA this thread issued must be complete before TMEM is freed
       // and before the peer CTA (whose shared memory the MMAs read) exits.
@@ -236,8 +273,10 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
-    const uint32_t quarter = warp & 3u;  // TMEM lanes this warp may access
-    const uint32_t cstage0 = sC + (warp - 2u) * 2u * kCStageBytes;
+    const uint32_t e = warp - 2u;         // epilogue warp index
+    const uint32_t quarter = warp & 3u;   // TMEM lanes this warp may access
+    const uint32_t nblk = e >> 2;         // which 256-column block of the tile
+    const uint32_t cstage0 = sC + e * Cfg::kCBufs * kCStageBytes;
     const uint32_t tempty_leader0 = ptx::mapa(tempty0, 0);
     uint32_t acc = 0, acc_phase = 0, cbuf = 0;
     uint32_t next = (cluster < num_tiles) ? __ldg(p.tiles + cluster) : 0u;
@@ -249,25 +288,28 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
       ptx::tc_fence_after();
       const int row = static_cast<int>(tile >> 16) * kTileM + static_cast<int>(rank) * 128 +
                       static_cast<int>(quarter) * 32;
-      const int col0 = static_cast<int>(tile & 0xFFFFu) * kTileN;
-      const uint32_t t_row = tmem_base + ((quarter * 32u) << 16) + acc * kAccCols;
+      const int col0 = static_cast<int>(tile & 0xFFFFu) * Cfg::kTileN + static_cast<int>(nblk) * kBlockN;
+      const uint32_t t_row =
+          tmem_base + ((quarter * 32u) << 16) + acc * Cfg::kTileN + nblk * kBlockN;
+      // Chunks of 64 columns: TMEM -> registers -> bf16 -> swizzled staging
+      // buffer -> TMA store.  The other epilogue warps' chunks interleave.
 #pragma unroll 1
-      for (int c = 0; c < kTileN / kCBoxCols; ++c) {
-        uint32_t v0[32], v1[32];
-        ptx::tmem_ld_32x32b_x32(t_row + c * kCBoxCols, v0);
-        ptx::tmem_ld_32x32b_x32(t_row + c * kCBoxCols + 32, v1);
+      for (int c = 0; c < kBlockN / kCBoxCols; ++c) {
+        uint32_t cur[64];
+        ptx::tmem_ld_32x32b_x32(t_row + c * kCBoxCols, *reinterpret_cast<uint32_t(*)[32]>(&cur[0]));
+        ptx::tmem_ld_32x32b_x32(t_row + c * kCBoxCols + 32,
+                                *reinterpret_cast<uint32_t(*)[32]>(&cur[32]));
         ptx::tmem_wait_ld();
-        if (c == kTileN / kCBoxCols - 1) {
-          // Whole accumulator is in registers: hand it back to the MMA warp.
+        ptx::reg_fence64(cur);
+        if (c == kBlockN / kCBoxCols - 1) {
+          // This warp's part of the accumulator is in registers: release it.
           ptx::tc_fence_before();
           __syncwarp();
           if (lane == 0) ptx::mbar_arrive_cluster(tempty_leader0 + 8 * acc);
         }
         uint32_t pk[32];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) pk[i] = ptx::pack_bf16x2(v0[2 * i], v0[2 * i + 1]);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) pk[16 + i] = ptx::pack_bf16x2(v1[2 * i], v1[2 * i + 1]);
+        for (int i = 0; i < 32; ++i) pk[i] = ptx::pack_bf16x2(cur[2 * i], cur[2 * i + 1]);
         const int col = col0 + c * kCBoxCols;
         const bool store = (row < p.M) && (col < p.N);  // warp-uniform
         // TMA clips the innermost dimension in 16-byte units, so a chunk that
@@ -287,8 +329,8 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
           }
         } else if (store) {
           const uint32_t buf = cstage0 + cbuf * kCStageBytes;
-          // The TMA store that last read this buffer (two stores ago) must be done reading.
-          if (lane == 0) ptx::bulk_wait_group_read<1>();
+          // The TMA store that last read this buffer must be done reading it.
+          if (lane == 0) ptx::bulk_wait_group_read<Cfg::kCBufs - 1>();
           __syncwarp();
           const uint32_t rowaddr = buf + lane * 128u;
 #pragma unroll
@@ -302,11 +344,13 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
             ptx::tma_store_2d(&map_c, buf, col, row);
             ptx::bulk_commit_group();
           }
-          cbuf ^= 1u;
+          if (++cbuf == Cfg::kCBufs) cbuf = 0;
         }
       }
-      acc ^= 1u;
-      if (acc == 0) acc_phase ^= 1u;
+      if (++acc == Cfg::kAccBufs) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
     }
     if (lane == 0) ptx::bulk_wait_group<0>();
     __syncwarp();

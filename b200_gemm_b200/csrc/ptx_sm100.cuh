@@ -232,6 +232,15 @@ __device__ __forceinline__ uint64_t policy_evict_normal() {
   asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
   return p;
 }
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+// 0 = evict_normal, 1 = evict_last, 2 = evict_first
+__device__ __forceinline__ uint64_t l2_policy(int kind) {
+  return kind == 1 ? policy_evict_last() : (kind == 2 ? policy_evict_first() : policy_evict_normal());
+}
 
 // --------------------------------------------------------------- tcgen05
 // TMEM allocation for a CTA pair: one warp of each CTA executes these.
@@ -295,6 +304,23 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
 
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Registers written by tcgen05.ld are only defined after tcgen05.wait::ld.
+// Passing them through an empty volatile asm placed after the wait makes
+// every later use depend on it, so no use can be scheduled above the wait.
+__device__ __forceinline__ void reg_fence32(uint32_t* r) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                 "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                 "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]),
+                 "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
+                 "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]),
+                 "+r"(r[30]), "+r"(r[31]));
+}
+__device__ __forceinline__ void reg_fence64(uint32_t (&r)[64]) {
+  reg_fence32(&r[0]);
+  reg_fence32(&r[32]);
 }
 
 // Two fp32 -> packed bf16x2 with round-to-nearest-even (lo in bits 0-15).

@@ -82,12 +82,33 @@ int b200gemm_run_kernel(int M, int N, int K, const void* A, const void* B, void*
  * both at compile time (NUM_SM = 148, matmul_1.cuh:19). */
 int b200gemm_device_info(b200gemm_t handle, int* sm_count, int* max_clusters);
 
-/* Host computation of the persistent tile schedule the kernel follows for a
- * tiles_m x tiles_n grid of 256 x 256 output tiles: out[0 .. tiles_m*tiles_n)
- * receives (tile_m << 16 | tile_n) in Hilbert-curve order; entry j runs on
- * cluster j mod (number of clusters).  The device builds the identical table.
- * Replaces createHilbert (include/hilbert.hpp:42-84).  Needs no GPU. */
-int b200gemm_schedule_host(unsigned int tiles_m, unsigned int tiles_n, unsigned int* out);
+/* Output tile width of the handle's GEMM calls: 256 (256 x 256 tiles, two
+ * TMEM accumulators so a tile's epilogue overlaps the next tile's MMAs), 512
+ * (256 x 512 tiles: one A stage feeds two MMAs, a quarter less operand
+ * traffic per flop), or 0 (default) to choose per call from the shape.
+ * The reference has one fixed 256 x 256 configuration (matmul_1.cuh:13-22). */
+int b200gemm_set_tile_width(b200gemm_t handle, int width);
+
+/* The tile width (256 or 512) a call with this shape would use now; 0 for
+ * an invalid handle or shape. */
+int b200gemm_tile_width_for(b200gemm_t handle, int M, int N, int K);
+
+/* Tile orders for the persistent schedule. */
+#define B200GEMM_ORDER_HILBERT 0 /* Hilbert curve over the tile grid           */
+#define B200GEMM_ORDER_BANDS 1   /* bands of `band` tile-rows, columns swept    */
+
+/* Select the order in which the handle's kernels start their 256 x 256
+ * output tiles (entry j of the order runs on cluster j mod clusters).
+ * Applies to calls made after it.  Replaces the fixed Hilbert table of the
+ * reference (createHilbert, include/hilbert.hpp:42-84). */
+int b200gemm_set_schedule(b200gemm_t handle, int order, int band);
+
+/* Host computation of the schedule for a tiles_m x tiles_n grid of
+ * 256 x 256 output tiles: out[0 .. tiles_m*tiles_n) receives
+ * (tile_m << 16 | tile_n) in start order.  The device builds the identical
+ * table.  Replaces createHilbert (include/hilbert.hpp:42-84).  Needs no GPU. */
+int b200gemm_schedule_host(unsigned int tiles_m, unsigned int tiles_n, int order, int band,
+                           unsigned int* out);
 
 /* Human-readable text for a status code (static storage). */
 const char* b200gemm_strerror(int code);

@@ -65,10 +65,18 @@ SHAPES = [
 ]
 
 
+@pytest.fixture(params=[256, 512], ids=["w256", "w512"])
+def width_handle(request, gpu_handle):
+    """The session handle forced to one tile width for the test."""
+    gpu_handle.set_tile_width(request.param)
+    yield gpu_handle
+    gpu_handle.set_tile_width(0)
+
+
 @pytest.mark.parametrize("M,N,K", SHAPES)
-def test_parity_vs_oracle(gpu_handle, oracle_mod, M, N, K):
+def test_parity_vs_oracle(width_handle, oracle_mod, M, N, K):
     A, B = data.host_operands(M, N, K, "normal", seed=M + 7 * N + 13 * K)
-    got = _run(gpu_handle, A, B)
+    got = _run(width_handle, A, B)
     ref = oracle_mod.gemm_f64(A, B)
     got_f = oracle_mod.bf16_to_f32(got)
     assert not np.isnan(got_f).any(), "unwritten output elements (NaN poison survived)"
@@ -80,12 +88,12 @@ def test_parity_vs_oracle(gpu_handle, oracle_mod, M, N, K):
 
 
 @pytest.mark.parametrize("M,N,K", [(256, 256, 64), (300, 520, 72), (1024, 768, 64)])
-def test_known_answer_exact(gpu_handle, oracle_mod, M, N, K):
+def test_known_answer_exact(width_handle, oracle_mod, M, N, K):
     rng = np.random.Generator(np.random.PCG64(M * N + K))
     a = rng.integers(-2, 3, size=(M, K)).astype(np.float32)
     b = rng.integers(-2, 3, size=(N, K)).astype(np.float32)
     exact = (a.astype(np.int64) @ b.astype(np.int64).T).astype(np.float32)
-    got = _run(gpu_handle, oracle_mod.f32_to_bf16(a), oracle_mod.f32_to_bf16(b))
+    got = _run(width_handle, oracle_mod.f32_to_bf16(a), oracle_mod.f32_to_bf16(b))
     assert np.array_equal(got, oracle_mod.f32_to_bf16(exact))
 
 
@@ -100,11 +108,11 @@ def test_identity_and_permutation(gpu_handle, oracle_mod):
     assert np.array_equal(_run(gpu_handle, A, P), A[:, perm])
 
 
-def test_ldc_column_slice(gpu_handle, oracle_mod):
+def test_ldc_column_slice(width_handle, oracle_mod):
     """C written into a column window of a wider matrix; the rest untouched."""
     M, N, K, ldc = 300, 264, 128, 1024
     A, B = data.host_operands(M, N, K, "uniform", seed=9)
-    got = _run(gpu_handle, A, B, ldc=ldc)
+    got = _run(width_handle, A, B, ldc=ldc)
     assert np.all(got[:, N:] == NAN_BF16)
     ref = oracle_mod.gemm_f64(A, B)
     assert oracle_mod.within_tolerance(oracle_mod.bf16_to_f32(got[:, :N]), ref).all()
@@ -118,6 +126,17 @@ def test_k_zero_writes_zeros(gpu_handle):
     assert rc == _lib.OK
     torch.cuda.synchronize()
     assert np.all(_host_bits(C) == 0)
+
+
+def test_tile_width_selection(gpu_handle):
+    h = gpu_handle
+    assert h.tile_width_for(8192, 8192, 8192) in (256, 512)
+    assert h.tile_width_for(256, 256, 64) == 256  # one tile: the narrow tile wastes nothing
+    h.set_tile_width(512)
+    assert h.tile_width_for(256, 256, 64) == 512
+    h.set_tile_width(0)
+    with pytest.raises(Exception):
+        h.set_tile_width(384)
 
 
 def test_device_info(gpu_handle):
@@ -215,6 +234,20 @@ def test_8192_vs_cublaslt_and_sampled_oracle(gpu_handle, oracle_mod):
     ref = oracle_mod.gemm_sampled(A_bits, B_bits, rows, cols)
     got = oracle_mod.bf16_to_f32(_host_bits(C)[rows, cols])
     assert oracle_mod.within_tolerance(got, ref).all()
+
+
+@pytest.mark.parametrize("width", [256, 512])
+def test_8192_widths_agree(gpu_handle, width):
+    """Both tile widths give bit-identical results (same per-element K order)."""
+    M = N = K = 8192
+    A, B = data.device_operands(M, N, K, "normal", seed=4)
+    gpu_handle.set_tile_width(256)
+    C1 = gpu_handle.bf16_nt(A, B)
+    gpu_handle.set_tile_width(width)
+    C2 = gpu_handle.bf16_nt(A, B)
+    gpu_handle.set_tile_width(0)
+    torch.cuda.synchronize()
+    assert torch.equal(C1.view(torch.int16), C2.view(torch.int16))
 
 
 def test_full_size_properties(gpu_handle):
