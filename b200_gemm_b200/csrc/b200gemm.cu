@@ -25,10 +25,10 @@ namespace b200gemm {
 #define B200GEMM_STAGES_N512 4
 #endif
 #ifndef B200GEMM_DEFAULT_ORDER
-#define B200GEMM_DEFAULT_ORDER 0
+#define B200GEMM_DEFAULT_ORDER 1
 #endif
 #ifndef B200GEMM_DEFAULT_BAND
-#define B200GEMM_DEFAULT_BAND 8
+#define B200GEMM_DEFAULT_BAND 16
 #endif
 using CfgN256 = GemmCfg<B200GEMM_STAGES_N256, 1>;  // 256 x 256 tiles, overlapped epilogue
 using CfgN512 = GemmCfg<B200GEMM_STAGES_N512, 2>;  // 256 x 512 tiles, shared A stage
@@ -72,9 +72,10 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 }
 
 // Row-major bf16 matrix [outer x inner] with a row pitch in bytes, read or
-// written in boxes of [box_outer x box_inner] through the 128-byte swizzle.
+// written in boxes of [box_outer x box_inner] through a shared-memory swizzle.
 bool encode_2d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer,
-               uint64_t pitch_bytes, uint32_t box_inner, uint32_t box_outer) {
+               uint64_t pitch_bytes, uint32_t box_inner, uint32_t box_outer,
+               CUtensorMapSwizzle swizzle) {
   auto encode = tensor_map_encoder();
   if (encode == nullptr) return false;
   cuuint64_t dims[2] = {inner, outer};
@@ -83,7 +84,7 @@ bool encode_2d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer
   cuuint32_t elem_strides[2] = {1, 1};
   const CUresult r =
       encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box,
-             elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -308,10 +309,14 @@ int maps_for(b200gemm_t h, int M, int N, int K, const void* A, const void* B, vo
     }
     slot->valid = false;
     const uint64_t k = static_cast<uint64_t>(K);
-    if (!encode_2d(&slot->map_a, A, k, static_cast<uint64_t>(M), k * 2, kBlockK, 128) ||
-        !encode_2d(&slot->map_b, B, k, static_cast<uint64_t>(N), k * 2, kBlockK, 128) ||
+    // A, B: 64 x 128 boxes (one 128-byte K row per operand row), 128-byte
+    // swizzle as the MMA descriptors expect; C: 32 x 32 boxes, 64-byte swizzle.
+    if (!encode_2d(&slot->map_a, A, k, static_cast<uint64_t>(M), k * 2, kBlockK, 128,
+                   CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_2d(&slot->map_b, B, k, static_cast<uint64_t>(N), k * 2, kBlockK, 128,
+                   CU_TENSOR_MAP_SWIZZLE_128B) ||
         !encode_2d(&slot->map_c, C, static_cast<uint64_t>(N), static_cast<uint64_t>(M),
-                   static_cast<uint64_t>(ldc) * 2, kCBoxCols, kCBoxRows)) {
+                   static_cast<uint64_t>(ldc) * 2, kCBoxCols, kCBoxRows, CU_TENSOR_MAP_SWIZZLE_64B)) {
       return B200GEMM_ERR_CUDA;
     }
     slot->a = A;

@@ -37,8 +37,9 @@
 #define B200GEMM_L2_POLICY_A 0
 #endif
 #ifndef B200GEMM_L2_POLICY_B
-#define B200GEMM_L2_POLICY_B 0
+#define B200GEMM_L2_POLICY_B 1
 #endif
+
 
 namespace b200gemm {
 
@@ -49,9 +50,9 @@ constexpr int kMmaK = 16;         // K per tcgen05.mma (kind::f16)
 constexpr int kTmemCols = 512;    // the whole TMEM of the SM
 constexpr int kStageBytesA = 128 * kBlockK * 2;       // A rows of one CTA, one stage
 constexpr int kBlockBytesB = 128 * kBlockK * 2;       // B rows of one CTA for one N block
-constexpr int kCBoxCols = 64;     // one 128-byte row of bf16
+constexpr int kCBoxCols = 32;     // one 64-byte row of bf16 (64-byte swizzle)
 constexpr int kCBoxRows = 32;     // one warp's TMEM lane quarter
-constexpr int kCStageBytes = kCBoxCols * kCBoxRows * 2;
+constexpr int kCStageBytes = kCBoxCols * kCBoxRows * 2;  // 2 KB staging buffer
 
 // Watchdog sites (reported in status word 1).
 enum : unsigned int {
@@ -89,7 +90,7 @@ struct GemmCfg {
   static constexpr int kAccBufs = kTmemCols / kTileN;
   static constexpr int kEpiWarps = 4 * NB;
   static constexpr int kThreads = 64 + 32 * kEpiWarps;
-  static constexpr int kCBufs = (NB == 1) ? 2 : 1;   // staging buffers per epilogue warp
+  static constexpr int kCBufs = 2;   // staging buffers per epilogue warp
   static constexpr int kStageBytesB = kBlockBytesB * NB;
   static constexpr uint32_t kTxBytes = 2 * (kStageBytesA + kStageBytesB);  // both CTAs
   // shared memory layout (offsets from a 1024-byte aligned base)
@@ -123,6 +124,52 @@ constexpr uint64_t kSmemDescHi = (uint64_t(1024 >> 4) << 32) | (uint64_t(1) << 1
 
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
   return kSmemDescHi | uint64_t((addr & 0x3FFFFu) >> 4);
+}
+
+// Write one 32-row x 32-column chunk of C held as packed bf16 pairs (lane =
+// row, pk[i] = columns 2i, 2i+1).  Full chunks go through a 64-byte-swizzled
+// staging buffer (16-byte group j of row r sits at group j ^ ((r >> 1) & 3),
+// so the eight rows of each shared-memory wavefront hit distinct banks) and a
+// TMA store.  TMA clips the innermost dimension in 16-byte units, so the
+// chunk that ends inside a 16-byte group (N % 8 != 0) is written with plain
+// per-element predicated stores instead.
+template <class Cfg>
+__device__ __forceinline__ void store_c_chunk(const uint32_t (&pk)[16], int col, int row,
+                                              uint32_t lane, uint32_t cstage0, uint32_t& cbuf,
+                                              const CUtensorMap& map_c, const GemmParams& p) {
+  const bool store = (row < p.M) && (col < p.N);  // warp-uniform
+  const bool ragged = ((p.N & 7) != 0) && (col + kCBoxCols > p.N);
+  if (store && ragged) {
+    const int r = row + static_cast<int>(lane);
+    if (r < p.M) {
+      uint16_t* dst = p.C + static_cast<long long>(r) * p.ldc + col;
+      const int ncols = p.N - col;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        if (2 * i < ncols) dst[2 * i] = static_cast<uint16_t>(pk[i] & 0xFFFFu);
+        if (2 * i + 1 < ncols) dst[2 * i + 1] = static_cast<uint16_t>(pk[i] >> 16);
+      }
+    }
+  } else if (store) {
+    const uint32_t buf = cstage0 + cbuf * kCStageBytes;
+    // The TMA store that last read this buffer (two chunks ago) must be done.
+    if (lane == 0) ptx::bulk_wait_group_read<Cfg::kCBufs - 1>();
+    __syncwarp();
+    const uint32_t rowaddr = buf + lane * 64u;
+    const uint32_t sw = (lane >> 1) & 3u;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      ptx::st_shared_v4(rowaddr + ((static_cast<uint32_t>(j) ^ sw) << 4), pk[4 * j], pk[4 * j + 1],
+                        pk[4 * j + 2], pk[4 * j + 3]);
+    }
+    ptx::fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      ptx::tma_store_2d(&map_c, buf, col, row);
+      ptx::bulk_commit_group();
+    }
+    if (++cbuf == Cfg::kCBufs) cbuf = 0;
+  }
 }
 
 template <class Cfg>
@@ -291,61 +338,24 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
       const int col0 = static_cast<int>(tile & 0xFFFFu) * Cfg::kTileN + static_cast<int>(nblk) * kBlockN;
       const uint32_t t_row =
           tmem_base + ((quarter * 32u) << 16) + acc * Cfg::kTileN + nblk * kBlockN;
-      // Chunks of 64 columns: TMEM -> registers -> bf16 -> swizzled staging
-      // buffer -> TMA store.  The other epilogue warps' chunks interleave.
+      // Chunks of 32 columns: TMEM -> registers -> bf16 -> swizzled staging
+      // buffer -> TMA store, two staging buffers in flight per warp.
 #pragma unroll 1
       for (int c = 0; c < kBlockN / kCBoxCols; ++c) {
-        uint32_t cur[64];
-        ptx::tmem_ld_32x32b_x32(t_row + c * kCBoxCols, *reinterpret_cast<uint32_t(*)[32]>(&cur[0]));
-        ptx::tmem_ld_32x32b_x32(t_row + c * kCBoxCols + 32,
-                                *reinterpret_cast<uint32_t(*)[32]>(&cur[32]));
+        uint32_t cur[32];
+        ptx::tmem_ld_32x32b_x32(t_row + c * kCBoxCols, cur);
         ptx::tmem_wait_ld();
-        ptx::reg_fence64(cur);
+        ptx::reg_fence32(cur);
         if (c == kBlockN / kCBoxCols - 1) {
           // This warp's part of the accumulator is in registers: release it.
           ptx::tc_fence_before();
           __syncwarp();
           if (lane == 0) ptx::mbar_arrive_cluster(tempty_leader0 + 8 * acc);
         }
-        uint32_t pk[32];
+        uint32_t pk[16];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) pk[i] = ptx::pack_bf16x2(cur[2 * i], cur[2 * i + 1]);
-        const int col = col0 + c * kCBoxCols;
-        const bool store = (row < p.M) && (col < p.N);  // warp-uniform
-        // TMA clips the innermost dimension in 16-byte units, so a chunk that
-        // ends inside a 16-byte group (N % 8 != 0) is written with plain,
-        // per-element predicated stores instead.
-        const bool ragged = ((p.N & 7) != 0) && (col + kCBoxCols > p.N);
-        if (store && ragged) {
-          const int r = row + static_cast<int>(lane);
-          if (r < p.M) {
-            uint16_t* dst = p.C + static_cast<long long>(r) * p.ldc + col;
-            const int ncols = p.N - col;
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              if (2 * i < ncols) dst[2 * i] = static_cast<uint16_t>(pk[i] & 0xFFFFu);
-              if (2 * i + 1 < ncols) dst[2 * i + 1] = static_cast<uint16_t>(pk[i] >> 16);
-            }
-          }
-        } else if (store) {
-          const uint32_t buf = cstage0 + cbuf * kCStageBytes;
-          // The TMA store that last read this buffer must be done reading it.
-          if (lane == 0) ptx::bulk_wait_group_read<Cfg::kCBufs - 1>();
-          __syncwarp();
-          const uint32_t rowaddr = buf + lane * 128u;
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            ptx::st_shared_v4(rowaddr + ((static_cast<uint32_t>(j) ^ (lane & 7u)) << 4), pk[4 * j],
-                              pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
-          }
-          ptx::fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            ptx::tma_store_2d(&map_c, buf, col, row);
-            ptx::bulk_commit_group();
-          }
-          if (++cbuf == Cfg::kCBufs) cbuf = 0;
-        }
+        for (int i = 0; i < 16; ++i) pk[i] = ptx::pack_bf16x2(cur[2 * i], cur[2 * i + 1]);
+        store_c_chunk<Cfg>(pk, col0 + c * kCBoxCols, row, lane, cstage0, cbuf, map_c, p);
       }
       if (++acc == Cfg::kAccBufs) {
         acc = 0;
