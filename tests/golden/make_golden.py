@@ -9,6 +9,7 @@ reference kernel computes C, and the bf16 output bits are saved as
 (matmul_1.cuh:390), so each case runs in a fresh process.
 
     python tests/golden/make_golden.py <outdir>
+    python tests/golden/make_golden.py time 8192     # reference kernel TFLOPS
 
 The reference only supports M, N multiples of 256 and K multiples of 64,
 so the cases respect that.
@@ -55,7 +56,43 @@ def run_case(name: str, outdir: Path) -> None:
     print(f"{name}: ok")
 
 
+def time_reference(size: int, reps: int = 20) -> None:
+    """Throughput of the reference kernel itself at size^3 (U[-1,1] operands),
+    back-to-back launches timed with CUDA events, as its bench does
+    (matmul_b200.cu:139-153).  Printed as one JSON line."""
+    import json
+
+    import torch
+
+    from b200_gemm_b200 import data
+
+    lib = ctypes.CDLL(str(ROOT / "oracle" / "_ref" / "libref_gemm.so"))
+    lib.ref_run_kernel1.restype = ctypes.c_int
+    lib.ref_run_kernel1.argtypes = [ctypes.c_int] * 3 + [ctypes.c_void_p] * 3
+    A, B = data.device_operands(size, size, size, "uniform", seed=1)
+    C = torch.empty(size, size, dtype=torch.bfloat16, device="cuda")
+    run = lambda: lib.ref_run_kernel1(size, size, size, A.data_ptr(), B.data_ptr(), C.data_ptr())
+    for _ in range(3):
+        if run() != 0:
+            raise SystemExit("reference launch failed")
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    ref = torch.matmul(A, B.t())
+    ok = bool(((C.float() - ref.float()).abs() <= 2.0 ** -7 * (ref.float().abs() + 1.0)).all())
+    print(json.dumps({"kernel": "reference runKernel1", "size": size, "ms": ms,
+                      "tflops": 2.0 * size ** 3 / ms / 1e9, "matches_cublaslt": ok}))
+
+
 def main() -> int:
+    if len(sys.argv) > 1 and sys.argv[1] == "time":
+        time_reference(int(sys.argv[2]) if len(sys.argv) > 2 else 8192)
+        return 0
     outdir = Path(sys.argv[1]) if len(sys.argv) > 1 else Path(__file__).resolve().parent
     outdir.mkdir(parents=True, exist_ok=True)
     if len(sys.argv) > 2:
