@@ -39,6 +39,7 @@ SIGNATURES = {
     "b200gemm_tile_width_for": (_c_int, [_vp, _c_int, _c_int, _c_int]),
     "b200gemm_set_schedule": (_c_int, [_vp, _c_int, _c_int]),
     "b200gemm_schedule_host": (_c_int, [_c_uint, _c_uint, _c_int, _c_int, ctypes.POINTER(_c_uint)]),
+    "b200gemm_bf16_nt_noalloc": (_c_int, [_c_int, _c_int, _c_int, _vp, _vp, _vp, _c_int, _vp]),
     "b200gemm_strerror": (ctypes.c_char_p, [_c_int]),
     "b200gemm_version": (_c_int, []),
 }

@@ -493,3 +493,140 @@ extern "C" int b200gemm_run_kernel(int M, int N, int K, const void* A, const voi
   }
   return b200gemm_bf16_nt(h, M, N, K, A, B, C, N, nullptr);
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free entry point.
+//
+// Some callers cannot call cudaMalloc (or anything that allocates device
+// memory) on the path that runs a GEMM: a memory-pool or caching-allocator
+// implementation that calls the GEMM from inside its own bookkeeping, a
+// serving process that plans all device memory at start-up and must not
+// allocate afterwards (an allocation can block on the device, fail under
+// fragmentation, or invalidate the plan), or code that cannot own a handle.
+// b200gemm_bf16_nt_noalloc serves them: the caller passes A, B and C, and the
+// only other device memory it touches is the fixed array below, compiled into
+// this library.  Every GPU that loads the library holds the array until the
+// process exits.
+namespace {
+
+constexpr uint32_t kNoAllocStatusWords = 64;   // 4 used; pads the table to a 256-byte boundary
+constexpr uint32_t kNoAllocMaxTiles = 16384;   // largest tile grid one call may use
+
+struct NoAllocDevice {
+  bool ready = false;
+  uint32_t* scratch = nullptr;  // device address of no_alloc_scratch on this device
+  int clusters_n256 = 0;
+  int clusters_n512 = 0;
+};
+
+constexpr int kNoAllocMaxDevices = 64;
+NoAllocDevice no_alloc_devices[kNoAllocMaxDevices];
+std::mutex no_alloc_mu;
+
+}  // namespace
+
+// Status words followed by the tile schedule of the most recent call, shared
+// by every call on the device.  In host code this name only stands for the
+// symbol; its device address comes from cudaGetSymbolAddress.
+static __device__ __align__(256) uint32_t no_alloc_scratch[kNoAllocStatusWords + kNoAllocMaxTiles];
+
+extern "C" int b200gemm_bf16_nt_noalloc(int M, int N, int K, const void* A, const void* B, void* C,
+                                        int ldc, void* stream_ptr) {
+  if (M < 0 || N < 0 || K < 0) return B200GEMM_ERR_INVALID_ARG;
+  if (M == 0 || N == 0) return B200GEMM_OK;
+  if (C == nullptr || (K > 0 && (A == nullptr || B == nullptr))) return B200GEMM_ERR_INVALID_ARG;
+  if (ldc < N || (ldc % 8) != 0 || (K % 8) != 0) return B200GEMM_ERR_UNSUPPORTED;
+  if (!aligned16(C) || (K > 0 && (!aligned16(A) || !aligned16(B)))) return B200GEMM_ERR_UNSUPPORTED;
+  const uint32_t tiles_m = static_cast<uint32_t>((M + kTileM - 1) / kTileM);
+  if (tiles_m > 0xFFFFu || static_cast<uint32_t>((N + kBlockN - 1) / kBlockN) > 0xFFFFu)
+    return B200GEMM_ERR_TOO_LARGE;
+
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return B200GEMM_ERR_NO_DEVICE;
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return B200GEMM_ERR_NO_DEVICE;
+  NoAllocDevice st;
+  {
+    // One-time set-up per device, on the first call with that device current.
+    std::lock_guard<std::mutex> lock(no_alloc_mu);
+    NoAllocDevice& d = no_alloc_devices[dev];
+    if (!d.ready) {
+      int major = 0, minor = 0, sms = 0;
+      if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+          cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess ||
+          cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+        return B200GEMM_ERR_CUDA;
+      }
+      if (major != 10 || minor != 0) return B200GEMM_ERR_NO_DEVICE;
+      if (tensor_map_encoder() == nullptr) return B200GEMM_ERR_CUDA;
+      void* ptr = nullptr;
+      if (cudaGetSymbolAddress(&ptr, no_alloc_scratch) != cudaSuccess || ptr == nullptr) {
+        cudaGetLastError();
+        return B200GEMM_ERR_CUDA;
+      }
+      const int c256 = prepare_kernel<CfgN256>(sms);
+      const int c512 = prepare_kernel<CfgN512>(sms);
+      if (c256 <= 0 || c512 <= 0) return B200GEMM_ERR_CUDA;
+      d.scratch = static_cast<uint32_t*>(ptr);
+      d.clusters_n256 = c256;
+      d.clusters_n512 = c512;
+      d.ready = true;
+    }
+    st = d;
+  }
+
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  if (K == 0) {  // empty sum: C = 0
+    return cudaMemset2DAsync(C, static_cast<size_t>(ldc) * 2, 0, static_cast<size_t>(N) * 2,
+                             static_cast<size_t>(M), stream) == cudaSuccess
+               ? B200GEMM_OK
+               : B200GEMM_ERR_CUDA;
+  }
+
+  const int num_kb = (K + kBlockK - 1) / kBlockK;
+  const int width = tile_plan_cost(2, tiles_m, N, num_kb, st.clusters_n512) <
+                            tile_plan_cost(1, tiles_m, N, num_kb, st.clusters_n256)
+                        ? 512
+                        : 256;
+  const uint32_t tiles_n = static_cast<uint32_t>((N + width - 1) / width);
+  const uint64_t tiles = static_cast<uint64_t>(tiles_m) * tiles_n;
+  if (tiles > kNoAllocMaxTiles) return B200GEMM_ERR_TOO_LARGE;  // beyond the static table
+
+  CUtensorMap ma, mb, mc;
+  const uint64_t k = static_cast<uint64_t>(K);
+  if (!encode_2d(&ma, A, k, static_cast<uint64_t>(M), k * 2, kBlockK, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_2d(&mb, B, k, static_cast<uint64_t>(N), k * 2, kBlockK, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_2d(&mc, C, static_cast<uint64_t>(N), static_cast<uint64_t>(M),
+                 static_cast<uint64_t>(ldc) * 2, kCBoxCols, kCBoxRows, CU_TENSOR_MAP_SWIZZLE_64B)) {
+    return B200GEMM_ERR_CUDA;
+  }
+
+  // The array keeps the previous call's contents: the status words must
+  // start at zero and the schedule is rewritten for this tile grid.
+  uint32_t* status = st.scratch;
+  uint32_t* table = st.scratch + kNoAllocStatusWords;
+  if (cudaMemsetAsync(status, 0, 4 * sizeof(uint32_t), stream) != cudaSuccess) return B200GEMM_ERR_CUDA;
+  build_schedule_kernel<<<1, 1024, 0, stream>>>(tiles_m, tiles_n, B200GEMM_DEFAULT_ORDER,
+                                                B200GEMM_DEFAULT_BAND, table);
+  if (cudaGetLastError() != cudaSuccess) return B200GEMM_ERR_CUDA;
+
+  GemmParams p;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.num_kb = num_kb;
+  p.num_tiles = static_cast<int>(tiles);
+  p.tiles = table;
+  p.status = status;
+  p.timeout_ns = kDefaultTimeoutNs;
+  p.C = static_cast<uint16_t*>(C);
+  p.ldc = ldc;
+  cudaError_t e;
+  if (width == 512) {
+    const int clusters = p.num_tiles < st.clusters_n512 ? p.num_tiles : st.clusters_n512;
+    e = launch_gemm<CfgN512>(clusters, stream, ma, mb, mc, p);
+  } else {
+    const int clusters = p.num_tiles < st.clusters_n256 ? p.num_tiles : st.clusters_n256;
+    e = launch_gemm<CfgN256>(clusters, stream, ma, mb, mc, p);
+  }
+  return e == cudaSuccess ? B200GEMM_OK : B200GEMM_ERR_CUDA;
+}

@@ -110,6 +110,31 @@ int b200gemm_set_schedule(b200gemm_t handle, int order, int band);
 int b200gemm_schedule_host(unsigned int tiles_m, unsigned int tiles_n, int order, int band,
                            unsigned int* out);
 
+/* C = A . B^T like b200gemm_bf16_nt (same layouts, alignment and K/ldc
+ * rules, asynchronous on `stream`, current device), for callers that must
+ * not allocate device memory on the GEMM path: a memory pool or caching
+ * allocator that runs GEMMs inside its own bookkeeping, a server that plans
+ * all device memory up front and may not allocate later (an allocation can
+ * block on the device or fail under fragmentation), or code that cannot
+ * keep a handle.  It takes no handle and calls no cudaMalloc/cudaFree or
+ * other allocating routine; its scratch (status words and the tile schedule)
+ * is one static array of 64 KB + 256 B inside this library, which every GPU
+ * that loads the library keeps until exit.
+ *  - Limit: the output may need at most 16384 tiles (256 x 256 or 256 x 512,
+ *    chosen per shape; e.g. 32768 x 32768 fits); larger problems return
+ *    B200GEMM_ERR_TOO_LARGE before any GPU work.
+ *  - The first call on a device sets up that device (looks up the array's
+ *    device address, sets kernel attributes); make it before any stream
+ *    capture.
+ *  - All calls share the array, which keeps the last call's contents; each
+ *    call clears the status words and rewrites the schedule on `stream`, so
+ *    calls that overlap on the GPU (different streams, not ordered) race.
+ *  - Device-side watchdog timeouts are recorded in the array only; they are
+ *    not reported through this call.
+ * No counterpart in the reference. */
+int b200gemm_bf16_nt_noalloc(int M, int N, int K, const void* A, const void* B, void* C, int ldc,
+                             void* stream);
+
 /* Human-readable text for a status code (static storage). */
 const char* b200gemm_strerror(int code);
 
