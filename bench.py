@@ -55,7 +55,13 @@ def parse_args(argv=None):
     p.add_argument("--steps", type=int, default=50)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--workload", default="square8192", choices=sorted(WORKLOADS))
-    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--impl", default="ours", choices=["ours", "reference", "cublaslt"],
+                   help="ours: this library; reference: the reference arithmetic on the host CPU; "
+                        "cublaslt: torch.matmul with the cuBLASLt backend on the same operands")
+    p.add_argument("--tile-width", type=int, default=0, choices=[0, 256, 512],
+                   help="force the output tile width (0 = the library's per-shape choice)")
+    p.add_argument("--order", default="default", choices=["default", "hilbert", "bands"])
+    p.add_argument("--band", type=int, default=16, help="tile-rows per band for --order bands")
     p.add_argument("--seed", type=int, default=1)
     p.add_argument("--allgather", action="store_true")
     p.add_argument("--no-cublas", action="store_true")
@@ -270,6 +276,10 @@ def run_ours(args, w):
     _, B = data.device_operands(8, Nl, K, w["dist"], seed=args.seed + 1 + n0, device=dev)
     C = torch.empty(M, Nl, dtype=torch.bfloat16, device=dev)
     gemm = Gemm(local)
+    if args.tile_width:
+        gemm.set_tile_width(args.tile_width)
+    if args.order != "default":
+        gemm.set_schedule(_lib.ORDER_HILBERT if args.order == "hilbert" else _lib.ORDER_BANDS, args.band)
     stream = torch.cuda.current_stream(dev)
     sptr = int(stream.cuda_stream)
     a_ptr, b_ptr, c_ptr = A.data_ptr(), B.data_ptr(), C.data_ptr()
@@ -278,6 +288,15 @@ def run_ours(args, w):
         rc = gemm.bf16_nt_ptr(M, Nl, K, a_ptr, b_ptr, c_ptr, Nl, sptr)
         if rc != _lib.OK:
             raise RuntimeError(_lib.strerror(rc))
+
+    library_arm = args.impl == "cublaslt"
+    if library_arm:
+        # Comparison arm: the same operands through cuBLASLt (no kernel of ours runs).
+        torch.backends.cuda.preferred_blas_library("cublaslt")
+        Bt = B.t()
+
+        def step():  # noqa: F811
+            torch.matmul(A, Bt, out=C)
 
     for _ in range(max(3, args.warmup)):
         step()
@@ -310,7 +329,7 @@ def run_ours(args, w):
 
     extra = {}
     # ------------------------------------------------ cuBLASLt on the same box
-    if not args.no_cublas:
+    if not args.no_cublas and not library_arm:
         torch.backends.cuda.preferred_blas_library("cublaslt")
         Cr = torch.empty_like(C)
         for _ in range(max(3, args.warmup)):
@@ -352,7 +371,7 @@ def run_ours(args, w):
         del gathered
 
     # ----------------------------------------------------- end to end (host)
-    if not args.no_e2e:
+    if not args.no_e2e and not library_arm:
         e2e = run_e2e(gemm, torch, dev, stream, M, Nl, K, A, B, args, barrier, distributed, world)
         extra["e2e"] = e2e
 
@@ -362,7 +381,7 @@ def run_ours(args, w):
     if rank == 0:
         peaks, peak_kind = load_peaks()
         peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
-        traffic = load_traffic(args.workload)
+        traffic = None if library_arm else load_traffic(args.workload)
         result = {
             "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
@@ -375,7 +394,7 @@ def run_ours(args, w):
                        "l2": ("operands larger than L2 (%.0f MB > 126 MB), no flush"
                               % ((M * K + Nl * K) * 2 / 1e6)) if (M * K + Nl * K) * 2 > L2_BYTES
                        else "operands fit in L2: NOT flushed"},
-            "gpu_launches": args.steps,
+            "gpu_launches": 0 if library_arm else args.steps,
             "launch": dict(info, threads_per_cta=192, cluster=2),
             "roofline": {"bound": "tensor", "achieved": kernel_tflops, "peak": peak, "unit": "TFLOP/s",
                          "frac": kernel_tflops / peak, "peak_kind": f"{peak_kind} bf16_tflops (burst)",
@@ -384,7 +403,12 @@ def run_ours(args, w):
             "clocks": clocks.summary(),
         }
         result.update(extra)
-        if not args.no_cpu_baseline:
+        if library_arm:
+            result["impl"] = "cublaslt"
+            result["tile_width"] = None
+        else:
+            result["tile_width"] = gemm.tile_width_for(M, Nl, K)
+        if not args.no_cpu_baseline and not library_arm:
             result["cpu_baseline"] = cpu_baseline(w, args.seed, args.cpu_seconds)
     gemm.close()
     if distributed:
