@@ -9,7 +9,8 @@
 //     status instead of spinning forever (reference `wait`, lines 451-463);
 //   * the leader-CTA barrier address comes from `mapa`, not from clearing
 //     bit 24 of the shared address (reference `mbar_cta0_addr`, line 66);
-//   * no TMA load here carries a cluster-multicast qualifier, so the library
+//   * every TMA load here lands in the issuing CTA only (none is broadcast to
+//     other CTAs of the cluster), so the library
 //     is safe to run on every GPU of a multi-GPU job.
 #pragma once
 
