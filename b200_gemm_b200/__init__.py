@@ -90,12 +90,40 @@ class Gemm:
         M, K = A.shape
         N = B.shape[0]
         if out is None:
-            out = torch.empty(M, N, device=A.device, dtype=torch.bfloat16)
+            # C rows must start on 16-byte boundaries: pad the pitch to a
+            # multiple of 8 elements and hand back the [M, N] view.
+            pitch = 8 * ((N + 7) // 8)
+            out = torch.empty(M, pitch, device=A.device, dtype=torch.bfloat16)[:, :N]
         if out.dtype != torch.bfloat16 or tuple(out.shape) != (M, N) or out.stride(1) != 1:
             raise ValueError("out must be a bf16 [M, N] row-major view")
-        ldc = out.stride(0) if M > 1 else max(N, 8 * ((N + 7) // 8))
+        ldc = out.stride(0) if M > 1 else 8 * ((N + 7) // 8)
         rc = self.bf16_nt_ptr(M, N, K, _ptr(A), _ptr(B), _ptr(out), ldc, _stream_ptr(stream))
         _lib.check(rc, "b200gemm_bf16_nt")
+        return out
+
+    def bf16_nt_host(self, A, B, out=None, stream=None):
+        """out[M, N] = A @ B^T with A, B, out in (preferably pinned) host memory.
+
+        Copies and GEMMs are pipelined on the device; completion is ordered on
+        `stream` (default: the current CUDA stream), so synchronise it before
+        reading `out`."""
+        import torch
+
+        if A.dtype != torch.bfloat16 or B.dtype != torch.bfloat16 or A.is_cuda or B.is_cuda:
+            raise TypeError("A and B must be host torch.bfloat16 tensors")
+        if A.dim() != 2 or B.dim() != 2 or A.shape[1] != B.shape[1]:
+            raise ValueError(f"shape mismatch: A {tuple(A.shape)}, B {tuple(B.shape)}")
+        A, B = A.contiguous(), B.contiguous()
+        M, K = A.shape
+        N = B.shape[0]
+        if out is None:
+            out = torch.empty(M, N, dtype=torch.bfloat16, pin_memory=True)
+        if out.is_cuda or out.dtype != torch.bfloat16 or tuple(out.shape) != (M, N) or out.stride(1) != 1:
+            raise ValueError("out must be a host bf16 [M, N] row-major view")
+        ldc = out.stride(0) if M > 1 else N
+        rc = self._lib.b200gemm_bf16_nt_host(self._h, M, N, K, _ptr(A), _ptr(B), _ptr(out), ldc,
+                                             _stream_ptr(stream))
+        _lib.check(rc, "b200gemm_bf16_nt_host")
         return out
 
     def set_tile_width(self, width: int) -> None:

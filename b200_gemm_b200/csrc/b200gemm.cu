@@ -33,7 +33,7 @@ namespace b200gemm {
 using CfgN256 = GemmCfg<B200GEMM_STAGES_N256, 1>;  // 256 x 256 tiles, overlapped epilogue
 using CfgN512 = GemmCfg<B200GEMM_STAGES_N512, 2>;  // 256 x 512 tiles, shared A stage
 constexpr int kVersion = 10000;  // 1.0.0
-constexpr int kMapCacheSize = 8;
+constexpr int kMapCacheSize = 32;   // the host-staged path uses one entry per row chunk
 constexpr size_t kScheduleCacheSize = 16;
 constexpr unsigned long long kDefaultTimeoutNs = 2000000000ull;
 
@@ -163,6 +163,20 @@ double tile_plan_cost(int nb, uint32_t tiles_m, int N, int num_kb, int clusters)
 
 using namespace b200gemm;
 
+// Device buffers, streams and events of b200gemm_bf16_nt_host (created on
+// first use, grown when a larger problem arrives).
+struct HostStaging {
+  void* dA = nullptr;
+  void* dB = nullptr;
+  void* dC = nullptr;
+  size_t capA = 0, capB = 0, capC = 0;
+  bool ready = false;
+  cudaStream_t s_h2d = nullptr, s_mma = nullptr, s_d2h = nullptr;
+  static constexpr int kMaxChunks = 16;
+  cudaEvent_t ev_start = nullptr, ev_b = nullptr, ev_done = nullptr;
+  cudaEvent_t ev_a[kMaxChunks] = {}, ev_c[kMaxChunks] = {};
+};
+
 struct b200gemm_handle {
   int device = 0;
   int sm_count = 0;
@@ -177,6 +191,8 @@ struct b200gemm_handle {
   std::mutex mu;
   uint64_t tick = 0;
   MapEntry maps[kMapCacheSize];
+  HostStaging staging;
+  std::mutex staging_mu;   // serialises b200gemm_bf16_nt_host calls on one handle
   std::vector<ScheduleEntry> schedules;
 };
 
@@ -237,6 +253,22 @@ extern "C" void b200gemm_destroy(b200gemm_t h) {
     cudaDeviceSynchronize();
     for (auto& s : h->schedules) cudaFree(s.dev);
     cudaFree(h->status_dev);
+    HostStaging& st = h->staging;
+    cudaFree(st.dA);
+    cudaFree(st.dB);
+    cudaFree(st.dC);
+    if (st.ready) {
+      cudaStreamDestroy(st.s_h2d);
+      cudaStreamDestroy(st.s_mma);
+      cudaStreamDestroy(st.s_d2h);
+      cudaEventDestroy(st.ev_start);
+      cudaEventDestroy(st.ev_b);
+      cudaEventDestroy(st.ev_done);
+      for (int i = 0; i < HostStaging::kMaxChunks; ++i) {
+        cudaEventDestroy(st.ev_a[i]);
+        cudaEventDestroy(st.ev_c[i]);
+      }
+    }
   }
   delete h;
 }
@@ -492,6 +524,111 @@ extern "C" int b200gemm_run_kernel(int M, int N, int K, const void* A, const voi
     h = handles[dev];
   }
   return b200gemm_bf16_nt(h, M, N, K, A, B, C, N, nullptr);
+}
+
+// ---------------------------------------------------------------------------
+// Host-resident operands.  The problem is cut into row chunks of A and C;
+// three streams overlap the host->device copies of A chunks, the GEMM of the
+// previous chunk and the device->host copy of the chunk before it.  B is
+// copied first because every chunk needs all of it.
+namespace {
+
+bool ensure_capacity(void** buf, size_t* cap, size_t bytes) {
+  if (*cap >= bytes) return true;
+  cudaFree(*buf);
+  *buf = nullptr;
+  *cap = 0;
+  if (cudaMalloc(buf, bytes) != cudaSuccess) return false;
+  *cap = bytes;
+  return true;
+}
+
+bool prepare_staging(HostStaging& st) {
+  if (st.ready) return true;
+  bool ok = cudaStreamCreateWithFlags(&st.s_h2d, cudaStreamNonBlocking) == cudaSuccess &&
+            cudaStreamCreateWithFlags(&st.s_mma, cudaStreamNonBlocking) == cudaSuccess &&
+            cudaStreamCreateWithFlags(&st.s_d2h, cudaStreamNonBlocking) == cudaSuccess &&
+            cudaEventCreateWithFlags(&st.ev_start, cudaEventDisableTiming) == cudaSuccess &&
+            cudaEventCreateWithFlags(&st.ev_b, cudaEventDisableTiming) == cudaSuccess &&
+            cudaEventCreateWithFlags(&st.ev_done, cudaEventDisableTiming) == cudaSuccess;
+  for (int i = 0; ok && i < HostStaging::kMaxChunks; ++i) {
+    ok = cudaEventCreateWithFlags(&st.ev_a[i], cudaEventDisableTiming) == cudaSuccess &&
+         cudaEventCreateWithFlags(&st.ev_c[i], cudaEventDisableTiming) == cudaSuccess;
+  }
+  st.ready = ok;
+  return ok;
+}
+
+}  // namespace
+
+extern "C" int b200gemm_bf16_nt_host(b200gemm_t h, int M, int N, int K, const void* hA,
+                                     const void* hB, void* hC, int ldc, void* stream_ptr) {
+  if (h == nullptr || M < 0 || N < 0 || K < 0) return B200GEMM_ERR_INVALID_ARG;
+  if (M == 0 || N == 0) return B200GEMM_OK;
+  if (hC == nullptr || (K > 0 && (hA == nullptr || hB == nullptr))) return B200GEMM_ERR_INVALID_ARG;
+  if (ldc < N || (K % 8) != 0) return B200GEMM_ERR_UNSUPPORTED;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  DeviceGuard guard(h->device);
+  if (!guard.ok()) return B200GEMM_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(h->staging_mu);
+  HostStaging& st = h->staging;
+  const size_t ldc_dev = (static_cast<size_t>(N) + 7) & ~static_cast<size_t>(7);
+  const size_t bytesA = static_cast<size_t>(M) * K * 2, bytesB = static_cast<size_t>(N) * K * 2;
+  const size_t bytesC = static_cast<size_t>(M) * ldc_dev * 2;
+  if (!prepare_staging(st) || !ensure_capacity(&st.dA, &st.capA, bytesA > 0 ? bytesA : 16) ||
+      !ensure_capacity(&st.dB, &st.capB, bytesB > 0 ? bytesB : 16) ||
+      !ensure_capacity(&st.dC, &st.capC, bytesC)) {
+    return B200GEMM_ERR_CUDA;
+  }
+  // Chunks: whole 256-row tiles, at most kMaxChunks of them, about 8 when M allows.
+  const int tiles_m = (M + kTileM - 1) / kTileM;
+  const int want = tiles_m < 8 ? tiles_m : 8;
+  const int chunk_tiles = (tiles_m + want - 1) / want;
+  const int chunk_rows = chunk_tiles * kTileM;
+  const int chunks = (M + chunk_rows - 1) / chunk_rows;
+  if (chunks > HostStaging::kMaxChunks) return B200GEMM_ERR_TOO_LARGE;
+
+  auto ok = [](cudaError_t e) { return e == cudaSuccess; };
+  // The staging buffers are reused: this call's copies wait for the previous
+  // call's last copy-out (a never-recorded event is already complete).
+  if (!ok(cudaStreamWaitEvent(st.s_h2d, st.ev_done, 0)) || !ok(cudaStreamWaitEvent(st.s_mma, st.ev_done, 0)))
+    return B200GEMM_ERR_CUDA;
+  if (!ok(cudaEventRecord(st.ev_start, stream)) || !ok(cudaStreamWaitEvent(st.s_h2d, st.ev_start, 0)) ||
+      !ok(cudaStreamWaitEvent(st.s_mma, st.ev_start, 0)) ||
+      !ok(cudaStreamWaitEvent(st.s_d2h, st.ev_start, 0))) {
+    return B200GEMM_ERR_CUDA;
+  }
+  if (bytesB > 0 && !ok(cudaMemcpyAsync(st.dB, hB, bytesB, cudaMemcpyHostToDevice, st.s_h2d)))
+    return B200GEMM_ERR_CUDA;
+  if (!ok(cudaEventRecord(st.ev_b, st.s_h2d)) || !ok(cudaStreamWaitEvent(st.s_mma, st.ev_b, 0)))
+    return B200GEMM_ERR_CUDA;
+  auto* dA = static_cast<uint8_t*>(st.dA);
+  auto* dC = static_cast<uint8_t*>(st.dC);
+  const auto* srcA = static_cast<const uint8_t*>(hA);
+  auto* dstC = static_cast<uint8_t*>(hC);
+  for (int i = 0; i < chunks; ++i) {
+    const int r0 = i * chunk_rows;
+    const int rows = (M - r0) < chunk_rows ? (M - r0) : chunk_rows;
+    const size_t a_off = static_cast<size_t>(r0) * K * 2;
+    if (K > 0 && !ok(cudaMemcpyAsync(dA + a_off, srcA + a_off, static_cast<size_t>(rows) * K * 2,
+                                     cudaMemcpyHostToDevice, st.s_h2d)))
+      return B200GEMM_ERR_CUDA;
+    if (!ok(cudaEventRecord(st.ev_a[i], st.s_h2d)) ||
+        !ok(cudaStreamWaitEvent(st.s_mma, st.ev_a[i], 0)))
+      return B200GEMM_ERR_CUDA;
+    const int rc = b200gemm_bf16_nt(h, rows, N, K, dA + a_off, st.dB, dC + r0 * ldc_dev * 2,
+                                    static_cast<int>(ldc_dev), st.s_mma);
+    if (rc != B200GEMM_OK) return rc;
+    if (!ok(cudaEventRecord(st.ev_c[i], st.s_mma)) ||
+        !ok(cudaStreamWaitEvent(st.s_d2h, st.ev_c[i], 0)) ||
+        !ok(cudaMemcpy2DAsync(dstC + static_cast<size_t>(r0) * ldc * 2, static_cast<size_t>(ldc) * 2,
+                              dC + r0 * ldc_dev * 2, ldc_dev * 2, static_cast<size_t>(N) * 2,
+                              static_cast<size_t>(rows), cudaMemcpyDeviceToHost, st.s_d2h)))
+      return B200GEMM_ERR_CUDA;
+  }
+  if (!ok(cudaEventRecord(st.ev_done, st.s_d2h)) || !ok(cudaStreamWaitEvent(stream, st.ev_done, 0)))
+    return B200GEMM_ERR_CUDA;
+  return B200GEMM_OK;
 }
 
 // ---------------------------------------------------------------------------

@@ -53,6 +53,19 @@ void b200gemm_destroy(b200gemm_t handle);
 int b200gemm_bf16_nt(b200gemm_t handle, int M, int N, int K, const void* A, const void* B,
                      void* C, int ldc, void* stream);
 
+/* C = A . B^T with A, B and C in host memory (pinned memory lets the copies
+ * overlap; pageable memory works but serialises).  The handle stages the
+ * operands in device buffers it owns (allocated on first use, grown when
+ * needed): B is copied first, then A and C move in row chunks of whole
+ * 256-row tiles on separate streams, so the copy of chunk i+1, the GEMM of
+ * chunk i and the copy-out of chunk i-1 overlap.  Asynchronous with respect
+ * to the host: completion is ordered on `stream`, and the host buffers must
+ * stay valid until then.  Calls on one handle are serialised.  ldc is the
+ * host row pitch of C (>= N); K % 8 == 0.  No reference counterpart (the
+ * reference bench copies synchronously, matmul_b200.cu:80-83, 107-110). */
+int b200gemm_bf16_nt_host(b200gemm_t handle, int M, int N, int K, const void* A, const void* B,
+                          void* C, int ldc, void* stream);
+
 /* Waits for the handle's device, returns the first device-side error the
  * kernels recorded since the last call (B200GEMM_OK or
  * B200GEMM_ERR_DEVICE_TIMEOUT) and clears it.  `detail`, if non-null,
