@@ -133,6 +133,14 @@ class Gemm:
     def tile_width_for(self, M: int, N: int, K: int) -> int:
         return int(self._lib.b200gemm_tile_width_for(self._h, M, N, K))
 
+    def set_small_m(self, mode: int) -> None:
+        """-1/1: use the small-M kernel for eligible shapes (default); 0: never."""
+        _lib.check(self._lib.b200gemm_set_small_m(self._h, int(mode)), "b200gemm_set_small_m")
+
+    def small_m_split(self, M: int, N: int, K: int) -> int:
+        """K split of the small-M kernel for this shape, or 0 if the tiled kernel runs."""
+        return int(self._lib.b200gemm_small_m_split(self._h, M, N, K))
+
     def set_schedule(self, order: int, band: int = 8) -> None:
         """Tile start order: _lib.ORDER_HILBERT or _lib.ORDER_BANDS (band = tile-rows)."""
         _lib.check(self._lib.b200gemm_set_schedule(self._h, int(order), int(band)),

@@ -38,6 +38,8 @@ SIGNATURES = {
     "b200gemm_device_info": (_c_int, [_vp, ctypes.POINTER(_c_int), ctypes.POINTER(_c_int)]),
     "b200gemm_set_tile_width": (_c_int, [_vp, _c_int]),
     "b200gemm_tile_width_for": (_c_int, [_vp, _c_int, _c_int, _c_int]),
+    "b200gemm_set_small_m": (_c_int, [_vp, _c_int]),
+    "b200gemm_small_m_split": (_c_int, [_vp, _c_int, _c_int, _c_int]),
     "b200gemm_set_schedule": (_c_int, [_vp, _c_int, _c_int]),
     "b200gemm_schedule_host": (_c_int, [_c_uint, _c_uint, _c_int, _c_int, ctypes.POINTER(_c_uint)]),
     "b200gemm_bf16_nt_noalloc": (_c_int, [_c_int, _c_int, _c_int, _vp, _vp, _vp, _c_int, _vp]),

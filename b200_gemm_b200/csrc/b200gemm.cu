@@ -12,6 +12,7 @@
 #include <vector>
 
 #include "b200gemm.h"
+#include "gemm_decode_sm100.cuh"
 #include "gemm_sm100.cuh"
 #include "schedule.cuh"
 
@@ -135,6 +136,36 @@ int prepare_kernel(int sm_count) {
   return clusters;
 }
 
+// Small-M instances (K split over 1, 2 or 4 CTA pairs of one cluster).
+template <class Cfg>
+bool prepare_decode_kernel() {
+  if (cudaFuncSetAttribute(gemm_bf16_nt_decode_sm100<Cfg>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return true;
+}
+
+template <class Cfg>
+cudaError_t launch_decode(cudaStream_t stream, const CUtensorMap& ma, const CUtensorMap& mb,
+                          const CUtensorMap& mc, const DecodeParams& p) {
+  const unsigned clusters = static_cast<unsigned>((p.N + 255) / 256);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = Cfg::kClusterSize;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(clusters * Cfg::kClusterSize, 1, 1);
+  cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemm_bf16_nt_decode_sm100<Cfg>, ma, mb, mc, p);
+}
+
 template <class Cfg>
 cudaError_t launch_gemm(int clusters, cudaStream_t stream, const CUtensorMap& ma,
                         const CUtensorMap& mb, const CUtensorMap& mc, const GemmParams& p) {
@@ -184,6 +215,7 @@ struct b200gemm_handle {
   int clusters_n256 = 0;      // co-resident clusters of the 256-wide instance
   int clusters_n512 = 0;      // co-resident clusters of the 512-wide instance
   int tile_width = 0;         // 0 = choose per call, else 256 or 512
+  int small_m = -1;           // small-M kernel: -1 or 1 = use it when eligible, 0 = never
   unsigned int* status_dev = nullptr;
   unsigned long long timeout_ns = kDefaultTimeoutNs;
   int order = B200GEMM_DEFAULT_ORDER;      // tile order (schedule.cuh)
@@ -229,6 +261,10 @@ extern "C" int b200gemm_create(b200gemm_t* out, int device) {
   const int c256 = prepare_kernel<CfgN256>(prop.multiProcessorCount);
   const int c512 = prepare_kernel<CfgN512>(prop.multiProcessorCount);
   if (c256 <= 0 || c512 <= 0) return B200GEMM_ERR_CUDA;
+  if (!prepare_decode_kernel<DecodeCfg<1>>() || !prepare_decode_kernel<DecodeCfg<2>>() ||
+      !prepare_decode_kernel<DecodeCfg<4>>()) {
+    return B200GEMM_ERR_CUDA;
+  }
 
   auto* h = new b200gemm_handle();
   h->device = device;
@@ -385,8 +421,81 @@ int choose_tile_width(const b200gemm_handle* h, int M, int N, int K) {
 
 }  // namespace
 
+namespace {
+
+// K split for the small-M kernel, or 0 when the tiled kernel should run:
+// M <= 128, N % 8 == 0 (its C stores are whole 16-byte groups), and the
+// largest split in {4, 2, 1} whose clusters fit on the device in one wave
+// while every CTA pair keeps at least two K blocks.
+int decode_split(int M, int N, int K, int sm_count) {
+  if (M > 128 || (N % 8) != 0 || K < 2 * kBlockK) return 0;
+  const int clusters = (N + 255) / 256;
+  const int num_kb = (K + kBlockK - 1) / kBlockK;
+  for (int s : {4, 2}) {
+    if (clusters * 2 * s <= sm_count && num_kb >= 2 * s) return s;
+  }
+  return 1;
+}
+
+int run_decode(b200gemm_t h, int split, int M, int N, int K, const void* A, const void* B, void* C,
+               int ldc, cudaStream_t stream, unsigned long long timeout_ns) {
+  const uint64_t k = static_cast<uint64_t>(K);
+  CUtensorMap ma, mb, mc;
+  const uint32_t slice_rows = static_cast<uint32_t>(128 / split);
+  if (!encode_2d(&ma, A, k, static_cast<uint64_t>(M), k * 2, kBlockK, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_2d(&mb, B, k, static_cast<uint64_t>(N), k * 2, kBlockK, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_2d(&mc, C, static_cast<uint64_t>(N), static_cast<uint64_t>(M),
+                 static_cast<uint64_t>(ldc) * 2, 32, slice_rows, CU_TENSOR_MAP_SWIZZLE_NONE)) {
+    return B200GEMM_ERR_CUDA;
+  }
+  DecodeParams p;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.num_kb = (K + kBlockK - 1) / kBlockK;
+  p.kb_per_split = (p.num_kb + split - 1) / split;
+  p.status = h->status_dev;
+  p.timeout_ns = timeout_ns;
+  cudaError_t e;
+  if (split == 4) e = launch_decode<DecodeCfg<4>>(stream, ma, mb, mc, p);
+  else if (split == 2) e = launch_decode<DecodeCfg<2>>(stream, ma, mb, mc, p);
+  else e = launch_decode<DecodeCfg<1>>(stream, ma, mb, mc, p);
+  return e == cudaSuccess ? B200GEMM_OK : B200GEMM_ERR_CUDA;
+}
+
+}  // namespace
+
+extern "C" int b200gemm_small_m_split(b200gemm_t h, int M, int N, int K) {
+  if (h == nullptr || M <= 0 || N <= 0 || K < 0) return 0;
+  std::lock_guard<std::mutex> lock(h->mu);
+  return h->small_m != 0 ? decode_split(M, N, K, h->sm_count) : 0;
+}
+
+extern "C" int b200gemm_set_small_m(b200gemm_t h, int mode) {
+  if (h == nullptr || mode < -1 || mode > 1) return B200GEMM_ERR_INVALID_ARG;
+  std::lock_guard<std::mutex> lock(h->mu);
+  h->small_m = mode;
+  return B200GEMM_OK;
+}
+
+namespace {
+int gemm_device(b200gemm_t h, int M, int N, int K, const void* A, const void* B, void* C, int ldc,
+                void* stream_ptr, bool allow_small_m);
+}  // namespace
+
 extern "C" int b200gemm_bf16_nt(b200gemm_t h, int M, int N, int K, const void* A, const void* B,
                                 void* C, int ldc, void* stream_ptr) {
+  return gemm_device(h, M, N, K, A, B, C, ldc, stream_ptr, true);
+}
+
+namespace {
+
+// The device-pointer GEMM.  `allow_small_m` = false keeps a call on the
+// tiled kernel (used for the row chunks of a larger host-staged problem, so
+// chunking never changes which kernel, and hence which summation order, an
+// element gets).
+int gemm_device(b200gemm_t h, int M, int N, int K, const void* A, const void* B, void* C, int ldc,
+                void* stream_ptr, bool allow_small_m) {
   if (h == nullptr || M < 0 || N < 0 || K < 0) return B200GEMM_ERR_INVALID_ARG;
   if (M == 0 || N == 0) return B200GEMM_OK;
   if (C == nullptr || (K > 0 && (A == nullptr || B == nullptr))) return B200GEMM_ERR_INVALID_ARG;
@@ -405,6 +514,16 @@ extern "C" int b200gemm_bf16_nt(b200gemm_t h, int M, int N, int K, const void* A
                ? B200GEMM_OK
                : B200GEMM_ERR_CUDA;
   }
+
+  // Small M: stream B with every SM (operands swapped, K split in-cluster).
+  int split = 0;
+  unsigned long long decode_timeout;
+  {
+    std::lock_guard<std::mutex> lock(h->mu);
+    split = (allow_small_m && h->small_m != 0) ? decode_split(M, N, K, h->sm_count) : 0;
+    decode_timeout = h->timeout_ns;
+  }
+  if (split > 0) return run_decode(h, split, M, N, K, A, B, C, ldc, stream, decode_timeout);
 
   CUtensorMap ma, mb, mc;
   const uint32_t* sched = nullptr;
@@ -444,6 +563,8 @@ extern "C" int b200gemm_bf16_nt(b200gemm_t h, int M, int N, int K, const void* A
   }
   return e == cudaSuccess ? B200GEMM_OK : B200GEMM_ERR_CUDA;
 }
+
+}  // namespace
 
 extern "C" int b200gemm_set_tile_width(b200gemm_t h, int width) {
   if (h == nullptr || (width != 0 && width != 256 && width != 512)) return B200GEMM_ERR_INVALID_ARG;
@@ -616,8 +737,8 @@ extern "C" int b200gemm_bf16_nt_host(b200gemm_t h, int M, int N, int K, const vo
     if (!ok(cudaEventRecord(st.ev_a[i], st.s_h2d)) ||
         !ok(cudaStreamWaitEvent(st.s_mma, st.ev_a[i], 0)))
       return B200GEMM_ERR_CUDA;
-    const int rc = b200gemm_bf16_nt(h, rows, N, K, dA + a_off, st.dB, dC + r0 * ldc_dev * 2,
-                                    static_cast<int>(ldc_dev), st.s_mma);
+    const int rc = gemm_device(h, rows, N, K, dA + a_off, st.dB, dC + r0 * ldc_dev * 2,
+                               static_cast<int>(ldc_dev), st.s_mma, /*allow_small_m=*/M <= 128);
     if (rc != B200GEMM_OK) return rc;
     if (!ok(cudaEventRecord(st.ev_c[i], st.s_mma)) ||
         !ok(cudaStreamWaitEvent(st.s_d2h, st.ev_c[i], 0)) ||

@@ -106,6 +106,17 @@ int b200gemm_set_tile_width(b200gemm_t handle, int width);
  * an invalid handle or shape. */
 int b200gemm_tile_width_for(b200gemm_t handle, int M, int N, int K);
 
+/* Small-M kernel (M <= 128, N % 8 == 0, K >= 128): rows of B become the MMA's
+ * M side and K is split over 1, 2 or 4 CTA pairs of one cluster whose fp32
+ * partial sums are reduced through distributed shared memory, so every SM
+ * streams B from HBM.  mode -1 (default) or 1: use it for eligible shapes;
+ * 0: always use the tiled kernel.  The reference has no small-M path. */
+int b200gemm_set_small_m(b200gemm_t handle, int mode);
+
+/* The K split (1, 2 or 4) the small-M kernel would use for this shape on
+ * this handle, or 0 when the tiled kernel would run. */
+int b200gemm_small_m_split(b200gemm_t handle, int M, int N, int K);
+
 /* Tile orders for the persistent schedule. */
 #define B200GEMM_ORDER_HILBERT 0 /* Hilbert curve over the tile grid           */
 #define B200GEMM_ORDER_BANDS 1   /* bands of `band` tile-rows, columns swept    */

@@ -1,0 +1,90 @@
+"""Parity of the small-M (decode-shaped) kernel: rows of B on the MMA's M
+side, K split over 1, 2 or 4 CTA pairs of a cluster, partial sums reduced
+through distributed shared memory.  Compared with the fp64 oracle
+(|err| <= 2^-7 (|ref| + 1)) and, bit for bit where the K split is 1, with the
+tiled kernel."""
+import numpy as np
+import pytest
+
+from b200_gemm_b200 import _lib, data
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+def _dev(bits):
+    return torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).cuda().view(torch.bfloat16)
+
+
+def _bits(t):
+    return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+# (M, N, K, expected split)
+CASES = [
+    (128, 4096, 1024, 4),
+    (128, 8192, 512, 2),
+    (64, 16384, 256, 1),
+    (1, 512, 1024, 4),
+    (77, 2048, 1000, 4),    # ragged M and K
+    (128, 2048, 576, 4),    # 9 K blocks over 4 pairs: the last pair has none
+    (100, 1032, 384, 2),    # N not a multiple of 256: the last cluster is ragged
+]
+
+
+@pytest.mark.parametrize("M,N,K,split", CASES)
+def test_small_m_parity(gpu_handle, oracle_mod, M, N, K, split):
+    h = gpu_handle
+    assert h.small_m_split(M, N, K) == split
+    A_bits, B_bits = data.host_operands(M, N, K, "normal", seed=M * 7 + N + K)
+    A, B = _dev(A_bits), _dev(B_bits)
+    C = torch.full((M + 16, N), float("nan"), dtype=torch.bfloat16, device="cuda")
+    rc = h.bf16_nt_ptr(M, N, K, A.data_ptr(), B.data_ptr(), C.data_ptr(), N,
+                       torch.cuda.current_stream().cuda_stream)
+    assert rc == _lib.OK, _lib.strerror(rc)
+    torch.cuda.synchronize()
+    st, detail = h.last_device_status()
+    assert st == _lib.OK, detail
+    allc = _bits(C)
+    assert np.all(allc[M:] == 0x7FC0), "write past row M"
+    got = oracle_mod.bf16_to_f32(allc[:M])
+    ref = oracle_mod.gemm_f64(A_bits, B_bits)
+    ok = oracle_mod.within_tolerance(got, ref)
+    assert ok.all(), (np.argwhere(~ok)[:5], oracle_mod.max_scaled_error(got, ref))
+
+
+def test_small_m_unsplit_matches_tiled_bitwise(gpu_handle):
+    """With no K split the small-M kernel sums each element in the same K
+    order as the tiled kernel, so the two agree bit for bit."""
+    h = gpu_handle
+    M, N, K = 96, 16384, 512
+    assert h.small_m_split(M, N, K) == 1
+    A, B = data.device_operands(M, N, K, "normal", seed=5)
+    C1 = h.bf16_nt(A, B)
+    h.set_small_m(0)
+    try:
+        assert h.small_m_split(M, N, K) == 0
+        C2 = h.bf16_nt(A, B)
+    finally:
+        h.set_small_m(-1)
+    torch.cuda.synchronize()
+    assert torch.equal(C1.view(torch.int16), C2.view(torch.int16))
+
+
+def test_decode_config_vs_cublaslt(gpu_handle, oracle_mod):
+    """BASELINE decode config 128 x 8192 x 8192: every element vs cuBLASLt,
+    one full row vs the fp64 oracle."""
+    M, N, K = 128, 8192, 8192
+    A, B = data.device_operands(M, N, K, "normal", seed=7)
+    C = gpu_handle.bf16_nt(A, B)
+    torch.backends.cuda.preferred_blas_library("cublaslt")
+    R = torch.matmul(A, B.t())
+    torch.cuda.synchronize()
+    g, r = C.float(), R.float()
+    assert bool(((g - r).abs() <= 2.0 ** -7 * (r.abs() + 1.0)).all())
+    A_bits, B_bits = _bits(A), _bits(B)
+    rows = np.full(N, 77, dtype=np.int32)
+    cols = np.arange(N, dtype=np.int32)
+    ref = oracle_mod.gemm_sampled(A_bits, B_bits, rows, cols)
+    assert oracle_mod.within_tolerance(oracle_mod.bf16_to_f32(_bits(C)[77]), ref).all()
