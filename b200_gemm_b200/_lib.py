@@ -31,6 +31,11 @@ SIGNATURES = {
     "b200gemm_destroy": (None, [_vp]),
     "b200gemm_bf16_nt": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp, _vp, _vp, _c_int, _vp]),
     "b200gemm_bf16_nt_host": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp, _vp, _vp, _c_int, _vp]),
+    "b200gemm_bf16_nt_allgather": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp, _vp, _vp, _c_int,
+                                            ctypes.POINTER(_vp), _c_int, _vp]),
+    "b200gemm_ipc_get_handle": (_c_int, [_vp, _vp, ctypes.POINTER(_c_ull)]),
+    "b200gemm_ipc_open": (_c_int, [_vp, ctypes.POINTER(_vp)]),
+    "b200gemm_ipc_close": (_c_int, [_vp]),
     "b200gemm_last_device_status": (_c_int, [_vp, ctypes.POINTER(_c_uint)]),
     "b200gemm_set_timeout_ns": (_c_int, [_vp, _c_ull]),
     "b200gemm_selftest_watchdog": (_c_int, [_vp, _c_ull, _vp]),

@@ -480,12 +480,69 @@ extern "C" int b200gemm_set_small_m(b200gemm_t h, int mode) {
 
 namespace {
 int gemm_device(b200gemm_t h, int M, int N, int K, const void* A, const void* B, void* C, int ldc,
-                void* stream_ptr, bool allow_small_m);
+                void* stream_ptr, bool allow_small_m, int npeers = 0,
+                void* const* peers = nullptr);
 }  // namespace
 
 extern "C" int b200gemm_bf16_nt(b200gemm_t h, int M, int N, int K, const void* A, const void* B,
                                 void* C, int ldc, void* stream_ptr) {
   return gemm_device(h, M, N, K, A, B, C, ldc, stream_ptr, true);
+}
+
+extern "C" int b200gemm_bf16_nt_allgather(b200gemm_t h, int M, int N, int K, const void* A,
+                                          const void* B, void* C, int ldc, void* const* peer_C,
+                                          int npeers, void* stream_ptr) {
+  if (npeers < 0 || npeers > GemmParams::kMaxPeers || (npeers > 0 && peer_C == nullptr))
+    return B200GEMM_ERR_INVALID_ARG;
+  for (int i = 0; i < npeers; ++i) {
+    if (peer_C[i] == nullptr) return B200GEMM_ERR_INVALID_ARG;
+    if ((reinterpret_cast<uintptr_t>(peer_C[i]) & 15u) != 0) return B200GEMM_ERR_UNSUPPORTED;
+  }
+  if ((N % 8) != 0) return B200GEMM_ERR_UNSUPPORTED;  // peer rows are copied in 16-byte pieces
+  return gemm_device(h, M, N, K, A, B, C, ldc, stream_ptr, /*allow_small_m=*/false, npeers, peer_C);
+}
+
+extern "C" int b200gemm_ipc_get_handle(const void* dev_ptr, void* handle_out,
+                                       unsigned long long* offset_out) {
+  if (dev_ptr == nullptr || handle_out == nullptr || offset_out == nullptr)
+    return B200GEMM_ERR_INVALID_ARG;
+  // A handle names the whole allocation, so report where dev_ptr sits in it
+  // (a caching allocator may hand out pointers inside larger blocks).
+  static PFN_cuMemGetAddressRange_v3020 range_fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      range_fn = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(fn);
+    }
+  });
+  if (range_fn == nullptr) return B200GEMM_ERR_CUDA;
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range_fn(&base, &size, reinterpret_cast<CUdeviceptr>(dev_ptr)) != CUDA_SUCCESS)
+    return B200GEMM_ERR_CUDA;
+  cudaIpcMemHandle_t hnd;
+  if (cudaIpcGetMemHandle(&hnd, reinterpret_cast<void*>(base)) != cudaSuccess) return B200GEMM_ERR_CUDA;
+  static_assert(sizeof(hnd) <= B200GEMM_IPC_HANDLE_BYTES, "IPC handle size");
+  std::memcpy(handle_out, &hnd, sizeof(hnd));
+  *offset_out = static_cast<unsigned long long>(reinterpret_cast<CUdeviceptr>(dev_ptr) - base);
+  return B200GEMM_OK;
+}
+
+extern "C" int b200gemm_ipc_open(const void* handle, void** dev_ptr_out) {
+  if (handle == nullptr || dev_ptr_out == nullptr) return B200GEMM_ERR_INVALID_ARG;
+  cudaIpcMemHandle_t hnd;
+  std::memcpy(&hnd, handle, sizeof(hnd));
+  if (cudaIpcOpenMemHandle(dev_ptr_out, hnd, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
+    return B200GEMM_ERR_CUDA;
+  return B200GEMM_OK;
+}
+
+extern "C" int b200gemm_ipc_close(void* dev_ptr) {
+  if (dev_ptr == nullptr) return B200GEMM_ERR_INVALID_ARG;
+  return cudaIpcCloseMemHandle(dev_ptr) == cudaSuccess ? B200GEMM_OK : B200GEMM_ERR_CUDA;
 }
 
 namespace {
@@ -495,7 +552,7 @@ namespace {
 // chunking never changes which kernel, and hence which summation order, an
 // element gets).
 int gemm_device(b200gemm_t h, int M, int N, int K, const void* A, const void* B, void* C, int ldc,
-                void* stream_ptr, bool allow_small_m) {
+                void* stream_ptr, bool allow_small_m, int npeers, void* const* peers) {
   if (h == nullptr || M < 0 || N < 0 || K < 0) return B200GEMM_ERR_INVALID_ARG;
   if (M == 0 || N == 0) return B200GEMM_OK;
   if (C == nullptr || (K > 0 && (A == nullptr || B == nullptr))) return B200GEMM_ERR_INVALID_ARG;
@@ -552,6 +609,9 @@ int gemm_device(b200gemm_t h, int M, int N, int K, const void* A, const void* B,
   p.timeout_ns = timeout_ns;
   p.C = static_cast<uint16_t*>(C);
   p.ldc = ldc;
+  p.npeers = npeers;
+  for (int i = 0; i < GemmParams::kMaxPeers; ++i)
+    p.peer_c[i] = i < npeers ? static_cast<uint8_t*>(peers[i]) : nullptr;
 
   cudaError_t e;
   if (width == 512) {
@@ -878,6 +938,7 @@ extern "C" int b200gemm_bf16_nt_noalloc(int M, int N, int K, const void* A, cons
   p.timeout_ns = kDefaultTimeoutNs;
   p.C = static_cast<uint16_t*>(C);
   p.ldc = ldc;
+  p.npeers = 0;
   cudaError_t e;
   if (width == 512) {
     const int clusters = p.num_tiles < st.clusters_n512 ? p.num_tiles : st.clusters_n512;

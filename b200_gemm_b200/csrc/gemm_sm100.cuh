@@ -73,6 +73,12 @@ struct GemmParams {
   unsigned long long timeout_ns;
   uint16_t* C;                // C base (bf16 bits), for the ragged-N edge chunk
   long long ldc;              // C row pitch in elements
+  // Fused all-gather: every staged C chunk is also written to these peer
+  // copies of C (IPC-mapped device memory on other GPUs, same pitch ldc,
+  // already offset to this rank's first column).  npeers = 0 disables it.
+  static constexpr int kMaxPeers = 7;
+  int npeers;
+  uint8_t* peer_c[kMaxPeers];
 };
 
 // Compile-time shape of one kernel instance.
@@ -167,6 +173,22 @@ __device__ __forceinline__ void store_c_chunk(const uint32_t (&pk)[16], int col,
     if (lane == 0) {
       ptx::tma_store_2d(&map_c, buf, col, row);
       ptx::bulk_commit_group();
+    }
+    if (p.npeers > 0) {
+      // Copy the staged chunk to every peer's C over NVLink: 32 rows x 64 B =
+      // 128 segments of 16 B; four consecutive lanes write one row's 64 B.
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {
+        const uint32_t seg = static_cast<uint32_t>(it) * 32u + lane;
+        const uint32_t r = seg >> 2, q = seg & 3u;
+        uint32_t x0, x1, x2, x3;
+        ptx::ld_shared_v4(buf + r * 64u + ((q ^ ((r >> 1) & 3u)) << 4), x0, x1, x2, x3);
+        const int grow = row + static_cast<int>(r), gcol = col + static_cast<int>(q) * 8;
+        if (grow < p.M && gcol < p.N) {
+          const long long off = (static_cast<long long>(grow) * p.ldc + gcol) * 2;
+          for (int i = 0; i < p.npeers; ++i) ptx::st_global_v4(p.peer_c[i] + off, x0, x1, x2, x3);
+        }
+      }
     }
     if (++cbuf == Cfg::kCBufs) cbuf = 0;
   }
@@ -363,6 +385,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
       }
     }
     if (lane == 0) ptx::bulk_wait_group<0>();
+    if (p.npeers > 0) __threadfence_system();  // peer copies visible before the kernel ends
     __syncwarp();
   }
 

@@ -351,6 +351,14 @@ __device__ __forceinline__ void ld_shared_v4(uint32_t addr, uint32_t& a, uint32_
                : "memory");
 }
 
+// 16-byte store to global memory (local or a peer GPU's, through its
+// IPC/peer mapping).
+__device__ __forceinline__ void st_global_v4(void* ptr, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+  asm volatile("st.global.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(ptr), "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
+
 __device__ __forceinline__ void st_shared_u16(uint32_t addr, uint16_t v) {
   asm volatile("st.shared.u16 [%0], %1;" ::"r"(addr), "h"(v) : "memory");
 }

@@ -63,3 +63,74 @@ def max_over_ranks(value: float, device=None, group=None) -> float:
     t = torch.tensor([float(value)], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
     return float(t.item())
+
+
+class FusedAllGather:
+    """Full-width C on every rank, filled by one fused GEMM + all-gather.
+
+    Each rank allocates its own M x N C (row pitch rounded up to 8 elements),
+    shares it with the other ranks through CUDA IPC (handles exchanged with
+    one all_gather_object on the process group) and then calls
+    b200gemm_bf16_nt_allgather, whose epilogue writes every finished chunk of
+    this rank's column block into its own C and into every peer's C over
+    NVLink.  After `run` the caller's stream holds the completed writes; a
+    barrier among the ranks makes all blocks visible everywhere.
+    """
+
+    def __init__(self, gemm, M: int, N: int, group=None):
+        import ctypes
+
+        import torch
+        import torch.distributed as dist
+
+        from . import _lib
+
+        self._lib = _lib.load()
+        self.gemm = gemm
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world - 1 > 7:
+            raise ValueError("the fused all-gather writes to at most 7 peers")
+        self.M, self.N = M, N
+        self.pitch = 8 * ((N + 7) // 8)
+        self.n0, self.n1 = column_shard(N, self.world, self.rank)
+        if (self.n1 - self.n0) % 8 != 0:
+            raise ValueError("every column shard must be a multiple of 8 columns")
+        dev = torch.device("cuda", gemm.device)
+        self.C = torch.empty(M, self.pitch, dtype=torch.bfloat16, device=dev)
+        handle = (ctypes.c_char * 64)()
+        offset = ctypes.c_ulonglong()
+        _lib.check(self._lib.b200gemm_ipc_get_handle(self.C.data_ptr(), handle, ctypes.byref(offset)),
+                   "b200gemm_ipc_get_handle")
+        mine = (bytes(handle), int(offset.value))
+        everyone = [None] * self.world
+        dist.all_gather_object(everyone, mine, group=group)
+        self._opened = []
+        self.peer_bases = []
+        for r, (hbytes, off) in enumerate(everyone):
+            if r == self.rank:
+                continue
+            base = ctypes.c_void_p()
+            buf = (ctypes.c_char * 64).from_buffer_copy(hbytes)
+            _lib.check(self._lib.b200gemm_ipc_open(buf, ctypes.byref(base)), "b200gemm_ipc_open")
+            self._opened.append(base.value)
+            self.peer_bases.append(base.value + off)
+
+    def run(self, A, B_local, stream_ptr: int) -> int:
+        """C[:, n0:n1] = A @ B_local^T on every rank's C; returns the status."""
+        import ctypes
+
+        off = self.n0 * 2
+        peers = (ctypes.c_void_p * max(1, len(self.peer_bases)))(*[b + off for b in self.peer_bases])
+        K = A.shape[1]
+        return self._lib.b200gemm_bf16_nt_allgather(
+            self.gemm._h, self.M, self.n1 - self.n0, K, A.data_ptr(), B_local.data_ptr(),
+            self.C.data_ptr() + off, self.pitch, peers, len(self.peer_bases), stream_ptr)
+
+    def view(self):
+        return self.C[:, : self.N]
+
+    def close(self) -> None:
+        for base in self._opened:
+            self._lib.b200gemm_ipc_close(base)
+        self._opened = []

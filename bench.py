@@ -63,7 +63,10 @@ def parse_args(argv=None):
     p.add_argument("--order", default="default", choices=["default", "hilbert", "bands"])
     p.add_argument("--band", type=int, default=16, help="tile-rows per band for --order bands")
     p.add_argument("--seed", type=int, default=1)
-    p.add_argument("--allgather", action="store_true")
+    p.add_argument("--allgather", action="store_true",
+                   help="also time an NCCL all-gather of the C shards (separately)")
+    p.add_argument("--fused-allgather", action="store_true",
+                   help="also time the GEMM with the all-gather fused into its epilogue")
     p.add_argument("--no-cublas", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
@@ -411,6 +414,30 @@ def run_ours(args, w):
                               "algbw_gbs": nbytes / (ag_ms / 1e3) / 1e9,
                               "layout": "shard-major [world][M][N/world]", "timed_separately": True}
         del gathered
+
+    # ------------------------------- GEMM with the all-gather in its epilogue
+    if args.fused_allgather and distributed:
+        from b200_gemm_b200 import shard
+
+        fused = shard.FusedAllGather(gemm, M, Nl * world if w["scaling"] == "weak" else w["N"])
+        if fused.n1 - fused.n0 == Nl:
+            B_loc = B  # this rank's rows of B are exactly its column block
+            fstep = lambda: fused.run(A, B_loc, sptr)  # noqa: E731
+            for _ in range(3):
+                fstep()
+            barrier()
+            fms = time_steps(torch, fstep, max(3, min(args.steps, 20)), False, stream, dev, barrier)
+            t = torch.tensor([fms], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            reps = max(3, min(args.steps, 20))
+            fms = float(t.item()) / reps
+            extra["fused_allgather"] = {
+                "ms": fms, "tflops_aggregate": total_flops / (fms / 1e3) / 1e12,
+                "gemm_only_ms": ms_max / args.steps,
+                "bytes_to_peers_per_rank": 2 * M * Nl * (world - 1),
+                "how": "b200gemm_bf16_nt_allgather: epilogue stores each C chunk to all peers' "
+                       "full C over NVLink (IPC-mapped), timed with CUDA events, max over ranks"}
+        fused.close()
 
     # ----------------------------------------------------- end to end (host)
     if not args.no_e2e and not library_arm:

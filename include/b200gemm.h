@@ -66,6 +66,31 @@ int b200gemm_bf16_nt(b200gemm_t handle, int M, int N, int K, const void* A, cons
 int b200gemm_bf16_nt_host(b200gemm_t handle, int M, int N, int K, const void* A, const void* B,
                           void* C, int ldc, void* stream);
 
+/* GEMM with a fused all-gather of C for an N-sharded multi-GPU job (one
+ * process per GPU, each computing its own block of columns of C).  The call
+ * computes this rank's block into C like b200gemm_bf16_nt (C and ldc point at
+ * the block's place inside this rank's full-width C), and the epilogue also
+ * writes every finished 32 x 32 chunk straight into the same place of each
+ * peer's full-width C over NVLink (peer_C[i]: this rank's block inside peer
+ * i's C, same ldc; device pointers from b200gemm_ipc_open), so the gather
+ * overlaps the GEMM instead of following it.  npeers <= 7; N % 8 == 0.  When
+ * `stream` completes the local and peer writes are done; the peers still
+ * need a barrier with this rank before reading.  Always uses the tiled
+ * kernel.  No reference counterpart (the reference has no multi-GPU code). */
+int b200gemm_bf16_nt_allgather(b200gemm_t handle, int M, int N, int K, const void* A,
+                               const void* B, void* C, int ldc, void* const* peer_C, int npeers,
+                               void* stream);
+
+/* CUDA IPC helpers for sharing device buffers between the processes of a
+ * multi-GPU job: export a handle (B200GEMM_IPC_HANDLE_BYTES bytes) for the
+ * allocation holding dev_ptr plus dev_ptr's byte offset inside it, map a
+ * peer's handle (returns the allocation base; add the offset; peer access is
+ * enabled on first use), and unmap it. */
+#define B200GEMM_IPC_HANDLE_BYTES 64
+int b200gemm_ipc_get_handle(const void* dev_ptr, void* handle_out, unsigned long long* offset_out);
+int b200gemm_ipc_open(const void* handle, void** dev_ptr_out);
+int b200gemm_ipc_close(void* dev_ptr);
+
 /* Waits for the handle's device, returns the first device-side error the
  * kernels recorded since the last call (B200GEMM_OK or
  * B200GEMM_ERR_DEVICE_TIMEOUT) and clears it.  `detail`, if non-null,

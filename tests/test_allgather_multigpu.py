@@ -1,0 +1,83 @@
+"""Fused GEMM + all-gather across GPUs (b200gemm_bf16_nt_allgather): every
+rank computes its column block of C and its epilogue writes the block into
+every rank's full-width C over NVLink.  After a barrier each rank's C must
+equal, bit for bit, the single-GPU result of the whole GEMM (same kernel,
+same per-element K order).  Needs two or more GPUs; one process per GPU."""
+import os
+import socket
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, M, N, K, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    from b200_gemm_b200 import Gemm, data, shard
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        gemm = Gemm(rank)
+        A, B = data.device_operands(M, N, K, "normal", seed=11, device=f"cuda:{rank}")
+        fused = shard.FusedAllGather(gemm, M, N)
+        n0, n1 = fused.n0, fused.n1
+        B_local = B[n0:n1].contiguous()
+        fused.C.fill_(float("nan"))
+        torch.cuda.synchronize()
+        dist.barrier()
+        rc = fused.run(A, B_local, torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        dist.barrier()
+        full = gemm.bf16_nt(A, B)
+        torch.cuda.synchronize()
+        same = bool(torch.equal(fused.view().contiguous().view(torch.int16), full.contiguous().view(torch.int16)))
+        status = gemm.last_device_status()[0]
+        dist.barrier()
+        fused.close()
+        gemm.close()
+        q.put((rank, rc, same, status))
+    except Exception as e:  # report instead of hanging the parent
+        q.put((rank, -1, repr(e), -1))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("M,N,K", [(1024, 2048, 512), (600, 1536, 264)])
+def test_fused_allgather_matches_single_gpu(M, N, K):
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("needs at least two GPUs")
+    world = min(n, 8)
+    ctx = torch.multiprocessing.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, M, N, K, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    for _ in range(world):
+        r = q.get(timeout=300)
+        results[r[0]] = r[1:]
+    for p in procs:
+        p.join(timeout=120)
+        if p.is_alive():
+            p.kill()
+    for rank, (rc, same, status) in results.items():
+        assert rc == 0, (rank, rc, same)
+        assert same is True, (rank, same)
+        assert status == 0, (rank, status)
