@@ -126,6 +126,19 @@ class Gemm:
         _lib.check(rc, "b200gemm_bf16_nt_host")
         return out
 
+    def plan(self, M: int, N: int, K: int) -> dict:
+        """How a call with this shape would run on this handle now."""
+        out = (ctypes.c_int * 6)()
+        _lib.check(self._lib.b200gemm_plan(self._h, M, N, K, out), "b200gemm_plan")
+        kind = {1: "tiled", 2: "small_m"}.get(out[0], "?")
+        return {"kernel": kind, "tile_width": out[1], "tiles": out[2], "clusters": out[3],
+                "tail_split": out[4], "small_m_split": out[5]}
+
+    def set_tail_split(self, enable: bool) -> None:
+        """Split the last partial wave of tiles along K (default off)."""
+        _lib.check(self._lib.b200gemm_set_tail_split(self._h, 1 if enable else 0),
+                   "b200gemm_set_tail_split")
+
     def set_tile_width(self, width: int) -> None:
         """0 = choose per call (default), 256 or 512 output columns per tile."""
         _lib.check(self._lib.b200gemm_set_tile_width(self._h, int(width)), "b200gemm_set_tile_width")

@@ -41,6 +41,8 @@ SIGNATURES = {
     "b200gemm_selftest_watchdog": (_c_int, [_vp, _c_ull, _vp]),
     "b200gemm_run_kernel": (_c_int, [_c_int, _c_int, _c_int, _vp, _vp, _vp, ctypes.POINTER(_c_int)]),
     "b200gemm_device_info": (_c_int, [_vp, ctypes.POINTER(_c_int), ctypes.POINTER(_c_int)]),
+    "b200gemm_plan": (_c_int, [_vp, _c_int, _c_int, _c_int, ctypes.POINTER(_c_int)]),
+    "b200gemm_set_tail_split": (_c_int, [_vp, _c_int]),
     "b200gemm_set_tile_width": (_c_int, [_vp, _c_int]),
     "b200gemm_tile_width_for": (_c_int, [_vp, _c_int, _c_int, _c_int]),
     "b200gemm_set_small_m": (_c_int, [_vp, _c_int]),

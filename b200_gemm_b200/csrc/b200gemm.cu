@@ -37,6 +37,27 @@ constexpr int kVersion = 10000;  // 1.0.0
 constexpr int kMapCacheSize = 32;   // the host-staged path uses one entry per row chunk
 constexpr size_t kScheduleCacheSize = 16;
 constexpr unsigned long long kDefaultTimeoutNs = 2000000000ull;
+constexpr int kMaxTailCounters = 1024;   // two per split tile (one per CTA of the pair)
+constexpr int kMaxTailSplit = 6;
+
+// K split of the last, partial wave.  With T tiles on G clusters the last
+// wave has R = T mod G tiles and leaves G - R clusters idle; splitting each
+// of those tiles into S K slices (R * S <= G, at least 4 K blocks per slice,
+// S <= kMaxTailSplit because the last slice reads the other S - 1 partials)
+// shortens that wave to about 1/S of a tile.  Returns S (1 = no split).
+int tail_split_for(int tiles, int clusters, int num_kb) {
+  const int rem = tiles % clusters;  // a single partial wave is all tail
+  if (rem == 0) return 1;
+  int sk = clusters / rem;
+  if (sk > kMaxTailSplit) sk = kMaxTailSplit;
+  if (sk > num_kb / 4) sk = num_kb / 4;
+  while (sk >= 2) {
+    const int per = (num_kb + sk - 1) / sk;
+    if ((sk - 1) * per < num_kb) break;  // no empty slice
+    --sk;
+  }
+  return sk >= 2 ? sk : 1;
+}
 
 // Restores the caller's current device on scope exit.
 class DeviceGuard {
@@ -224,6 +245,15 @@ struct b200gemm_handle {
   uint64_t tick = 0;
   MapEntry maps[kMapCacheSize];
   HostStaging staging;
+  // K-split tail: fp32 partials of the last wave's split tiles and their
+  // tickets (zeroed once; the kernel resets each ticket after use).  Split
+  // launches share them, so each waits for the previous one (tail_event).
+  float* tail_ws = nullptr;
+  size_t tail_ws_bytes = 0;
+  unsigned int* tail_counters = nullptr;
+  cudaEvent_t tail_event = nullptr;
+  bool tail_event_recorded = false;
+  bool tail_split_enabled = false;  // off by default until its reduction beats the idle wave
   std::mutex staging_mu;   // serialises b200gemm_bf16_nt_host calls on one handle
   std::vector<ScheduleEntry> schedules;
 };
@@ -273,8 +303,12 @@ extern "C" int b200gemm_create(b200gemm_t* out, int device) {
   h->clusters_n512 = c512;
   h->max_clusters = c256 < c512 ? c256 : c512;
   if (cudaMalloc(&h->status_dev, 4 * sizeof(unsigned int)) != cudaSuccess ||
-      cudaMemset(h->status_dev, 0, 4 * sizeof(unsigned int)) != cudaSuccess) {
+      cudaMemset(h->status_dev, 0, 4 * sizeof(unsigned int)) != cudaSuccess ||
+      cudaMalloc(&h->tail_counters, kMaxTailCounters * sizeof(unsigned int)) != cudaSuccess ||
+      cudaMemset(h->tail_counters, 0, kMaxTailCounters * sizeof(unsigned int)) != cudaSuccess ||
+      cudaEventCreateWithFlags(&h->tail_event, cudaEventDisableTiming) != cudaSuccess) {
     cudaFree(h->status_dev);
+    cudaFree(h->tail_counters);
     delete h;
     return B200GEMM_ERR_CUDA;
   }
@@ -289,6 +323,9 @@ extern "C" void b200gemm_destroy(b200gemm_t h) {
     cudaDeviceSynchronize();
     for (auto& s : h->schedules) cudaFree(s.dev);
     cudaFree(h->status_dev);
+    cudaFree(h->tail_ws);
+    cudaFree(h->tail_counters);
+    if (h->tail_event != nullptr) cudaEventDestroy(h->tail_event);
     HostStaging& st = h->staging;
     cudaFree(st.dA);
     cudaFree(st.dB);
@@ -408,6 +445,8 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 }  // namespace
 
 namespace {
+
+bool tail_split_enabled_for(const b200gemm_handle* h) { return h->tail_split_enabled; }
 
 // Tile width (256 or 512 columns) a call on this handle will use.
 int choose_tile_width(const b200gemm_handle* h, int M, int N, int K) {
@@ -613,18 +652,92 @@ int gemm_device(b200gemm_t h, int M, int N, int K, const void* A, const void* B,
   for (int i = 0; i < GemmParams::kMaxPeers; ++i)
     p.peer_c[i] = i < npeers ? static_cast<uint8_t*>(peers[i]) : nullptr;
 
+  const int max_clusters = width == 512 ? h->clusters_n512 : h->clusters_n256;
+  const int clusters = p.num_tiles < max_clusters ? p.num_tiles : max_clusters;
+  // Split the last partial wave along K when it leaves clusters idle.
+  const int sk = tail_split_enabled_for(h) ? tail_split_for(p.num_tiles, clusters, p.num_kb) : 1;
+  p.tail_start = p.num_tiles;
+  p.tail_split = 1;
+  p.tail_kb = p.num_kb;
+  p.num_units = p.num_tiles;
+  p.workspace = nullptr;
+  p.tail_counters = nullptr;
+  bool tail_on = false;
+  if (sk >= 2) {
+    const int rem = p.num_tiles % clusters;
+    const size_t need = static_cast<size_t>(rem) * sk * 2 * 128 * width * sizeof(float);
+    std::lock_guard<std::mutex> lock(h->mu);
+    bool have_ws = h->tail_ws_bytes >= need;
+    if (!have_ws && 2 * rem <= kMaxTailCounters) {
+      cudaFree(h->tail_ws);  // waits for launches still using the old workspace
+      h->tail_ws = nullptr;
+      h->tail_ws_bytes = 0;
+      if (cudaMalloc(&h->tail_ws, need) == cudaSuccess) {
+        h->tail_ws_bytes = need;
+        have_ws = true;
+      }
+    }
+    if (have_ws && 2 * rem <= kMaxTailCounters) {
+      p.tail_start = p.num_tiles - rem;
+      p.tail_split = sk;
+      p.tail_kb = (p.num_kb + sk - 1) / sk;
+      p.num_units = p.tail_start + rem * sk;
+      p.workspace = h->tail_ws;
+      p.tail_counters = h->tail_counters;
+      tail_on = true;
+      if (h->tail_event_recorded && cudaStreamWaitEvent(stream, h->tail_event, 0) != cudaSuccess)
+        return B200GEMM_ERR_CUDA;
+    }
+  }
+
   cudaError_t e;
   if (width == 512) {
-    const int clusters = p.num_tiles < h->clusters_n512 ? p.num_tiles : h->clusters_n512;
     e = launch_gemm<CfgN512>(clusters, stream, ma, mb, mc, p);
   } else {
-    const int clusters = p.num_tiles < h->clusters_n256 ? p.num_tiles : h->clusters_n256;
     e = launch_gemm<CfgN256>(clusters, stream, ma, mb, mc, p);
+  }
+  if (e == cudaSuccess && tail_on) {
+    std::lock_guard<std::mutex> lock(h->mu);
+    if (cudaEventRecord(h->tail_event, stream) != cudaSuccess) return B200GEMM_ERR_CUDA;
+    h->tail_event_recorded = true;
   }
   return e == cudaSuccess ? B200GEMM_OK : B200GEMM_ERR_CUDA;
 }
 
 }  // namespace
+
+extern "C" int b200gemm_plan(b200gemm_t h, int M, int N, int K, int* plan) {
+  if (h == nullptr || plan == nullptr || M <= 0 || N <= 0 || K <= 0) return B200GEMM_ERR_INVALID_ARG;
+  std::lock_guard<std::mutex> lock(h->mu);
+  for (int i = 0; i < 6; ++i) plan[i] = 0;
+  const int split = h->small_m != 0 ? decode_split(M, N, K, h->sm_count) : 0;
+  if (split > 0) {
+    plan[0] = 2;  // small-M kernel
+    plan[1] = 256;
+    plan[2] = (N + 255) / 256;
+    plan[3] = plan[2];
+    plan[5] = split;
+    return B200GEMM_OK;
+  }
+  const int width = choose_tile_width(h, M, N, K);
+  const int tiles = ((M + kTileM - 1) / kTileM) * ((N + width - 1) / width);
+  const int maxc = width == 512 ? h->clusters_n512 : h->clusters_n256;
+  const int clusters = tiles < maxc ? tiles : maxc;
+  const int num_kb = (K + kBlockK - 1) / kBlockK;
+  plan[0] = 1;  // tiled kernel
+  plan[1] = width;
+  plan[2] = tiles;
+  plan[3] = clusters;
+  plan[4] = h->tail_split_enabled ? tail_split_for(tiles, clusters, num_kb) : 1;
+  return B200GEMM_OK;
+}
+
+extern "C" int b200gemm_set_tail_split(b200gemm_t h, int enable) {
+  if (h == nullptr) return B200GEMM_ERR_INVALID_ARG;
+  std::lock_guard<std::mutex> lock(h->mu);
+  h->tail_split_enabled = enable != 0;
+  return B200GEMM_OK;
+}
 
 extern "C" int b200gemm_set_tile_width(b200gemm_t h, int width) {
   if (h == nullptr || (width != 0 && width != 256 && width != 512)) return B200GEMM_ERR_INVALID_ARG;
@@ -933,6 +1046,12 @@ extern "C" int b200gemm_bf16_nt_noalloc(int M, int N, int K, const void* A, cons
   p.K = K;
   p.num_kb = num_kb;
   p.num_tiles = static_cast<int>(tiles);
+  p.num_units = p.num_tiles;  // no K-split tail on this path
+  p.tail_start = p.num_tiles;
+  p.tail_split = 1;
+  p.tail_kb = num_kb;
+  p.workspace = nullptr;
+  p.tail_counters = nullptr;
   p.tiles = table;
   p.status = status;
   p.timeout_ns = kDefaultTimeoutNs;

@@ -79,7 +79,44 @@ struct GemmParams {
   static constexpr int kMaxPeers = 7;
   int npeers;
   uint8_t* peer_c[kMaxPeers];
+  // Split of the last, partial wave: work units [0, tail_start) are whole
+  // tiles (tiles[u]); unit tail_start + r * tail_split + s is K slice s (of
+  // tail_kb K blocks) of tile tiles[tail_start + r].  A K slice writes its
+  // fp32 partial to workspace and takes a ticket from tail_counters; the last
+  // of a tile's slices adds the others to its own accumulator and stores C.
+  int num_units;        // tail_start + tail_tiles * tail_split
+  int tail_start;
+  int tail_split;       // 1 = no split
+  int tail_kb;
+  float* workspace;     // [tail unit][CTA of the pair][128 rows x tile width] fp32
+  unsigned int* tail_counters;  // [tail tile][CTA of the pair], zero between launches
 };
+
+// One work unit of a CTA pair: a tile and a K range; slot >= 0 marks a K
+// slice of a split tile (its index among the tail units).
+struct WorkUnit {
+  uint32_t tile;
+  int kb_begin, kb_end;
+  int slot;
+};
+
+__device__ __forceinline__ WorkUnit unit_at(const GemmParams& p, uint32_t u) {
+  WorkUnit w;
+  if (u < static_cast<uint32_t>(p.tail_start)) {
+    w.tile = __ldg(p.tiles + u);
+    w.kb_begin = 0;
+    w.kb_end = p.num_kb;
+    w.slot = -1;
+  } else {
+    const int v = static_cast<int>(u) - p.tail_start;
+    const int r = v / p.tail_split, sl = v - r * p.tail_split;
+    w.tile = __ldg(p.tiles + p.tail_start + r);
+    w.kb_begin = sl * p.tail_kb;
+    w.kb_end = min(p.num_kb, w.kb_begin + p.tail_kb);
+    w.slot = v;
+  }
+  return w;
+}
 
 // Compile-time shape of one kernel instance.
 //   NB = 1: a pair computes 256 x 256 tiles; TMEM holds two accumulators, so
@@ -110,7 +147,8 @@ struct GemmCfg {
   static constexpr int kDrain = kTEmpty + 8 * kAccBufs;
   static constexpr int kTmemSlot = kDrain + 8;
   static constexpr int kAbort = kTmemSlot + 4;
-  static constexpr int kEnd = kAbort + 4;
+  static constexpr int kTicket = kAbort + 4;     // "this CTA is the last K slice" flag
+  static constexpr int kEnd = kTicket + 4;
   static constexpr int kSmemBytes = kEnd + 1024;  // slack to align the base to 1024 B
   static_assert(kSmemBytes <= 232448, "exceeds the 227 KB per-CTA shared memory limit");
 };
@@ -248,8 +286,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
   uint32_t tmem_base;
   asm volatile("ld.shared.u32 %0, [%1];" : "=r"(tmem_base) : "r"(tmem_slot) : "memory");
 
-  const uint32_t num_tiles = static_cast<uint32_t>(p.num_tiles);
-  const int num_kb = p.num_kb;
+  const uint32_t num_units = static_cast<uint32_t>(p.num_units);
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -259,14 +296,15 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
       const uint32_t full_leader0 = ptx::mapa(full0, 0);
       uint32_t stage = 0, phase = 0;
       bool ok = true;
-      uint32_t next = (cluster < num_tiles) ? __ldg(p.tiles + cluster) : 0u;
-      for (uint32_t t = cluster; t < num_tiles && ok; t += nclusters) {
-        const uint32_t tile = next;
-        if (t + nclusters < num_tiles) next = __ldg(p.tiles + t + nclusters);
+      WorkUnit nxt = (cluster < num_units) ? unit_at(p, cluster) : WorkUnit{0, 0, 0, -1};
+      for (uint32_t t = cluster; t < num_units && ok; t += nclusters) {
+        const WorkUnit cur = nxt;
+        if (t + nclusters < num_units) nxt = unit_at(p, t + nclusters);
+        const uint32_t tile = cur.tile;
         const int row_a = static_cast<int>(tile >> 16) * kTileM + static_cast<int>(rank) * 128;
         const int row_b =
             static_cast<int>(tile & 0xFFFFu) * Cfg::kTileN + static_cast<int>(rank) * 128;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = cur.kb_begin; kb < cur.kb_end; ++kb) {
           if (!ptx::mbar_wait(empty0 + 8 * stage, phase ^ 1u, wd, kSiteProducer, t)) {
             ok = false;
             break;
@@ -294,11 +332,12 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
       const uint32_t own_tfull0 = ptx::mapa(tfull0, 0), peer_tfull0 = ptx::mapa(tfull0, 1);
       uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
       bool ok = true;
-      for (uint32_t t = cluster; t < num_tiles && ok; t += nclusters) {
+      for (uint32_t t = cluster; t < num_units && ok; t += nclusters) {
+        const WorkUnit cur = unit_at(p, t);
         if (!ptx::mbar_wait(tempty0 + 8 * acc, acc_phase ^ 1u, wd, kSiteMmaTmemEmpty, t)) break;
         ptx::tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * Cfg::kTileN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = cur.kb_begin; kb < cur.kb_end; ++kb) {
           if (!ptx::mbar_wait(full0 + 8 * stage, phase, wd, kSiteMmaFull, t)) {
             ok = false;
             break;
@@ -314,7 +353,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
               // second N block of B sits kBlockBytesB further on.
               ptx::mma_bf16_cg2(d_tmem + h * kBlockN, a_desc + 2 * k,
                                 b_desc + (h * kBlockBytesB >> 4) + 2 * k, kIdescBf16,
-                                (kb > 0 || k > 0) ? 1u : 0u);
+                                (kb > cur.kb_begin || k > 0) ? 1u : 0u);
             }
           }
           ptx::mma_commit_cg2(own_empty0 + 8 * stage);
@@ -348,36 +387,119 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
     const uint32_t cstage0 = sC + e * Cfg::kCBufs * kCStageBytes;
     const uint32_t tempty_leader0 = ptx::mapa(tempty0, 0);
     uint32_t acc = 0, acc_phase = 0, cbuf = 0;
-    uint32_t next = (cluster < num_tiles) ? __ldg(p.tiles + cluster) : 0u;
-    for (uint32_t t = cluster; t < num_tiles; t += nclusters) {
-      const uint32_t tile = next;
-      if (t + nclusters < num_tiles) next = __ldg(p.tiles + t + nclusters);
+    const uint32_t ticket = base + Cfg::kTicket;
+    WorkUnit nxt = (cluster < num_units) ? unit_at(p, cluster) : WorkUnit{0, 0, 0, -1};
+    for (uint32_t t = cluster; t < num_units; t += nclusters) {
+      const WorkUnit cur = nxt;
+      if (t + nclusters < num_units) nxt = unit_at(p, t + nclusters);
+      const uint32_t tile = cur.tile;
+      // After a timeout (here or in another role) the loop keeps running
+      // without doing work, so every epilogue warp still reaches every named
+      // barrier of the K-slice path below; later waits fail immediately.
       const bool full_ok = ptx::mbar_wait(tfull0 + 8 * acc, acc_phase, wd, kSiteEpilogue, t);
-      if (!__all_sync(0xFFFFFFFFu, full_ok)) break;  // keep the warp's decision uniform
+      const bool live = __all_sync(0xFFFFFFFFu, full_ok);  // warp-uniform
       ptx::tc_fence_after();
       const int row = static_cast<int>(tile >> 16) * kTileM + static_cast<int>(rank) * 128 +
                       static_cast<int>(quarter) * 32;
       const int col0 = static_cast<int>(tile & 0xFFFFu) * Cfg::kTileN + static_cast<int>(nblk) * kBlockN;
       const uint32_t t_row =
           tmem_base + ((quarter * 32u) << 16) + acc * Cfg::kTileN + nblk * kBlockN;
-      // Chunks of 32 columns: TMEM -> registers -> bf16 -> swizzled staging
-      // buffer -> TMA store, two staging buffers in flight per warp.
+      if (cur.slot < 0 && !live) {
+        // nothing to do for this tile
+      } else if (cur.slot < 0) {
+        // Whole tile: chunks of 32 columns: TMEM -> registers -> bf16 ->
+        // swizzled staging buffer -> TMA store, two buffers in flight per warp.
 #pragma unroll 1
-      for (int c = 0; c < kBlockN / kCBoxCols; ++c) {
-        uint32_t cur[32];
-        ptx::tmem_ld_32x32b_x32(t_row + c * kCBoxCols, cur);
-        ptx::tmem_wait_ld();
-        ptx::reg_fence32(cur);
-        if (c == kBlockN / kCBoxCols - 1) {
-          // This warp's part of the accumulator is in registers: release it.
-          ptx::tc_fence_before();
-          __syncwarp();
-          if (lane == 0) ptx::mbar_arrive_cluster(tempty_leader0 + 8 * acc);
-        }
-        uint32_t pk[16];
+        for (int c = 0; c < kBlockN / kCBoxCols; ++c) {
+          uint32_t v[32];
+          ptx::tmem_ld_32x32b_x32(t_row + c * kCBoxCols, v);
+          ptx::tmem_wait_ld();
+          ptx::reg_fence32(v);
+          if (c == kBlockN / kCBoxCols - 1) {
+            // This warp's part of the accumulator is in registers: release it.
+            ptx::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive_cluster(tempty_leader0 + 8 * acc);
+          }
+          uint32_t pk[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) pk[i] = ptx::pack_bf16x2(cur[2 * i], cur[2 * i + 1]);
-        store_c_chunk<Cfg>(pk, col0 + c * kCBoxCols, row, lane, cstage0, cbuf, map_c, p);
+          for (int i = 0; i < 16; ++i) pk[i] = ptx::pack_bf16x2(v[2 * i], v[2 * i + 1]);
+          store_c_chunk<Cfg>(pk, col0 + c * kCBoxCols, row, lane, cstage0, cbuf, map_c, p);
+        }
+      } else {
+        // K slice of a split tile.  Partials are laid out so that the 32
+        // threads of a warp (32 consecutive rows) touch 512 contiguous bytes
+        // per 16-byte column group: [column group][row 0..127] of float4.
+        const uint32_t i = quarter * 32u + lane;  // row of this CTA's 128
+        const int tile_r = cur.slot / p.tail_split;
+        const size_t slab = static_cast<size_t>(128) * Cfg::kTileN;  // floats per CTA per slice
+        auto part = [&](int slot) { return p.workspace + (static_cast<size_t>(slot) * 2 + rank) * slab; };
+        float* mine = part(cur.slot);
+#pragma unroll 1
+        for (int c = 0; c < (live ? kBlockN / kCBoxCols : 0); ++c) {
+          uint32_t v[32];
+          ptx::tmem_ld_32x32b_x32(t_row + c * kCBoxCols, v);
+          ptx::tmem_wait_ld();
+          ptx::reg_fence32(v);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const size_t g = static_cast<size_t>((nblk * (kBlockN / kCBoxCols) + c) * 8 + j);
+            ptx::st_global_v4(mine + (g * 128 + i) * 4, v[4 * j], v[4 * j + 1], v[4 * j + 2],
+                              v[4 * j + 3]);
+          }
+        }
+        // Ticket: the last K slice of this half-tile finishes it.
+        __threadfence();
+        ptx::named_barrier(1, 32 * Cfg::kEpiWarps);
+        if (threadIdx.x == 64) {
+          uint32_t last = 0u;
+          if (!ptx::aborted(wd)) {
+            const unsigned int old = atomicAdd(&p.tail_counters[tile_r * 2 + rank], 1u);
+            last = (old == static_cast<unsigned int>(p.tail_split - 1)) ? 1u : 0u;
+            if (last) p.tail_counters[tile_r * 2 + rank] = 0u;  // ready for the next launch
+          }
+          asm volatile("st.shared.u32 [%0], %1;" ::"r"(ticket), "r"(last) : "memory");
+        }
+        ptx::named_barrier(1, 32 * Cfg::kEpiWarps);
+        uint32_t is_last;
+        asm volatile("ld.shared.u32 %0, [%1];" : "=r"(is_last) : "r"(ticket) : "memory");
+        if (is_last && !ptx::aborted(wd)) {
+          __threadfence();
+          const int first = tile_r * p.tail_split;
+#pragma unroll 1
+          for (int c = 0; c < kBlockN / kCBoxCols; ++c) {
+            uint32_t v[32];
+            ptx::tmem_ld_32x32b_x32(t_row + c * kCBoxCols, v);
+            ptx::tmem_wait_ld();
+            ptx::reg_fence32(v);
+            float acc32[32];
+#pragma unroll
+            for (int k = 0; k < 32; ++k) acc32[k] = __uint_as_float(v[k]);
+#pragma unroll 1
+            for (int sl = 0; sl < p.tail_split; ++sl) {
+              if (first + sl == cur.slot) continue;
+              const float* other = part(first + sl);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const size_t g = static_cast<size_t>((nblk * (kBlockN / kCBoxCols) + c) * 8 + j);
+                uint32_t x0, x1, x2, x3;
+                ptx::ld_global_cg_v4(other + (g * 128 + i) * 4, x0, x1, x2, x3);
+                acc32[4 * j] += __uint_as_float(x0);
+                acc32[4 * j + 1] += __uint_as_float(x1);
+                acc32[4 * j + 2] += __uint_as_float(x2);
+                acc32[4 * j + 3] += __uint_as_float(x3);
+              }
+            }
+            uint32_t pk[16];
+#pragma unroll
+            for (int k = 0; k < 16; ++k)
+              pk[k] = ptx::pack_bf16x2(__float_as_uint(acc32[2 * k]), __float_as_uint(acc32[2 * k + 1]));
+            store_c_chunk<Cfg>(pk, col0 + c * kCBoxCols, row, lane, cstage0, cbuf, map_c, p);
+          }
+        }
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive_cluster(tempty_leader0 + 8 * acc);
       }
       if (++acc == Cfg::kAccBufs) {
         acc = 0;

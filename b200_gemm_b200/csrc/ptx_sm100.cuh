@@ -359,6 +359,20 @@ __device__ __forceinline__ void st_global_v4(void* ptr, uint32_t a, uint32_t b, 
                : "memory");
 }
 
+// 16-byte load cached in L2 only (data written by other SMs in this launch).
+__device__ __forceinline__ void ld_global_cg_v4(const void* ptr, uint32_t& a, uint32_t& b, uint32_t& c,
+                                                uint32_t& d) {
+  asm volatile("ld.global.cg.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(a), "=r"(b), "=r"(c), "=r"(d)
+               : "l"(ptr)
+               : "memory");
+}
+
+// Barrier over `count` threads (a multiple of 32) of this CTA on named barrier `id`.
+__device__ __forceinline__ void named_barrier(uint32_t id, uint32_t count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 __device__ __forceinline__ void st_shared_u16(uint32_t addr, uint16_t v) {
   asm volatile("st.shared.u16 [%0], %1;" ::"r"(addr), "h"(v) : "memory");
 }

@@ -127,6 +127,19 @@ int b200gemm_device_info(b200gemm_t handle, int* sm_count, int* max_clusters);
  * The reference has one fixed 256 x 256 configuration (matmul_1.cuh:13-22). */
 int b200gemm_set_tile_width(b200gemm_t handle, int width);
 
+/* Split the last, partial wave of tiles along K (default off): when T tiles
+ * leave the last wave of G clusters partly idle, each of its T mod G tiles is
+ * cut into up to 6 K slices run on the idle clusters; the slices write fp32
+ * partials to a workspace owned by the handle and the last one to finish
+ * adds them and writes C.  Split launches on one handle are serialised with
+ * an event (they share the workspace).  No reference counterpart. */
+int b200gemm_set_tail_split(b200gemm_t handle, int enable);
+
+/* Launch plan a call with this shape would use now, in plan[0..5]: kernel
+ * (1 tiled, 2 small-M), tile width, tiles, clusters launched, K split of the
+ * last partial wave (1 = none; tiled kernel), K split of the small-M kernel. */
+int b200gemm_plan(b200gemm_t handle, int M, int N, int K, int* plan);
+
 /* The tile width (256 or 512) a call with this shape would use now; 0 for
  * an invalid handle or shape. */
 int b200gemm_tile_width_for(b200gemm_t handle, int M, int N, int K);
