@@ -468,32 +468,46 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
           const int first = tile_r * p.tail_split;
 #pragma unroll 1
           for (int c = 0; c < kBlockN / kCBoxCols; ++c) {
-            uint32_t v[32];
-            ptx::tmem_ld_32x32b_x32(t_row + c * kCBoxCols, v);
-            ptx::tmem_wait_ld();
-            ptx::reg_fence32(v);
-            float acc32[32];
-#pragma unroll
-            for (int k = 0; k < 32; ++k) acc32[k] = __uint_as_float(v[k]);
-#pragma unroll 1
-            for (int sl = 0; sl < p.tail_split; ++sl) {
-              if (first + sl == cur.slot) continue;
-              const float* other = part(first + sl);
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const size_t g = static_cast<size_t>((nblk * (kBlockN / kCBoxCols) + c) * 8 + j);
-                uint32_t x0, x1, x2, x3;
-                ptx::ld_global_cg_v4(other + (g * 128 + i) * 4, x0, x1, x2, x3);
-                acc32[4 * j] += __uint_as_float(x0);
-                acc32[4 * j + 1] += __uint_as_float(x1);
-                acc32[4 * j + 2] += __uint_as_float(x2);
-                acc32[4 * j + 3] += __uint_as_float(x3);
-              }
-            }
+            // Sum the slices in slice order whichever slice arrives last, so
+            // the result does not depend on timing; this slice's own partial
+            // comes from TMEM at its place in the order.  Two 16-column halves
+            // keep the registers in check.
             uint32_t pk[16];
 #pragma unroll
-            for (int k = 0; k < 16; ++k)
-              pk[k] = ptx::pack_bf16x2(__float_as_uint(acc32[2 * k]), __float_as_uint(acc32[2 * k + 1]));
+            for (int hh = 0; hh < 2; ++hh) {
+              float acc16[16];
+#pragma unroll 1
+              for (int sl = 0; sl < p.tail_split; ++sl) {
+                float x[16];
+                if (first + sl == cur.slot) {
+                  uint32_t v[16];
+                  ptx::tmem_ld_32x32b_x16(t_row + c * kCBoxCols + hh * 16, v);
+                  ptx::tmem_wait_ld();
+                  ptx::reg_fence16(v);
+#pragma unroll
+                  for (int k = 0; k < 16; ++k) x[k] = __uint_as_float(v[k]);
+                } else {
+                  const float* other = part(first + sl);
+#pragma unroll
+                  for (int j = 0; j < 4; ++j) {
+                    const size_t g =
+                        static_cast<size_t>((nblk * (kBlockN / kCBoxCols) + c) * 8 + hh * 4 + j);
+                    uint32_t x0, x1, x2, x3;
+                    ptx::ld_global_cg_v4(other + (g * 128 + i) * 4, x0, x1, x2, x3);
+                    x[4 * j] = __uint_as_float(x0);
+                    x[4 * j + 1] = __uint_as_float(x1);
+                    x[4 * j + 2] = __uint_as_float(x2);
+                    x[4 * j + 3] = __uint_as_float(x3);
+                  }
+                }
+#pragma unroll
+                for (int k = 0; k < 16; ++k) acc16[k] = (sl == 0) ? x[k] : acc16[k] + x[k];
+              }
+#pragma unroll
+              for (int k = 0; k < 8; ++k)
+                pk[hh * 8 + k] = ptx::pack_bf16x2(__float_as_uint(acc16[2 * k]),
+                                                  __float_as_uint(acc16[2 * k + 1]));
+            }
             store_c_chunk<Cfg>(pk, col0 + c * kCBoxCols, row, lane, cstage0, cbuf, map_c, p);
           }
         }
