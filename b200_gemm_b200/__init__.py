@@ -140,7 +140,8 @@ class Gemm:
                    "b200gemm_set_tail_split")
 
     def set_tile_width(self, width: int) -> None:
-        """0 = choose per call (default), 256 or 512 output columns per tile."""
+        """0 = choose per call (default), or 512, 256, 224, 192, 128 output
+        columns per 256-row tile."""
         _lib.check(self._lib.b200gemm_set_tile_width(self._h, int(width)), "b200gemm_set_tile_width")
 
     def tile_width_for(self, M: int, N: int, K: int) -> int:

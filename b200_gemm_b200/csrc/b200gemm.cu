@@ -33,6 +33,21 @@ namespace b200gemm {
 #endif
 using CfgN256 = GemmCfg<B200GEMM_STAGES_N256, 1>;  // 256 x 256 tiles, overlapped epilogue
 using CfgN512 = GemmCfg<B200GEMM_STAGES_N512, 2>;  // 256 x 512 tiles, shared A stage
+// Narrower tiles for N that 256 does not divide into full waves (e.g. an
+// N-sharded projection with N = 1792 = 8 x 224); more stages fit because each
+// stage holds fewer B rows.
+using CfgN224 = GemmCfg<6, 1, 224>;
+using CfgN192 = GemmCfg<7, 1, 192>;
+using CfgN128 = GemmCfg<8, 1, 128>;
+// Tile widths of the tiled kernel, in the order the cost model prefers them
+// on a tie; index i of every per-width table below.
+constexpr int kWidths[] = {256, 512, 224, 192, 128};
+constexpr int kNumWidths = 5;
+inline int width_index(int width) {
+  for (int i = 0; i < kNumWidths; ++i)
+    if (kWidths[i] == width) return i;
+  return -1;
+}
 constexpr int kVersion = 10000;  // 1.0.0
 constexpr int kMapCacheSize = 32;   // the host-staged path uses one entry per row chunk
 constexpr size_t kScheduleCacheSize = 16;
@@ -117,6 +132,7 @@ struct MapEntry {
   const void* b = nullptr;
   void* c = nullptr;
   int M = 0, N = 0, K = 0, ldc = 0;
+  int b_rows = 0;   // rows of B's box: B rows one CTA loads per MMA column block
   uint64_t last_use = 0;
   CUtensorMap map_a, map_b, map_c;
 };
@@ -198,16 +214,28 @@ cudaError_t launch_gemm(int clusters, cudaStream_t stream, const CUtensorMap& ma
   return cudaLaunchKernelEx(&cfg, gemm_bf16_nt_sm100<Cfg>, ma, mb, mc, p);
 }
 
-// Relative cost of a GEMM with tiles of `nb` 256-column blocks: waves of
+// Relative cost of a GEMM with tiles `width` columns wide: waves of
 // persistent clusters times the time of one tile, in units of one 64-deep K
-// block of a 256 x 256 tile at full tensor rate.  The efficiencies are the
-// measured tensor-pipe activity of each instance on large problems; the
-// 512-wide tile also pays its non-overlapped epilogue (about 4 K blocks).
-double tile_plan_cost(int nb, uint32_t tiles_m, int N, int num_kb, int clusters) {
-  const uint64_t tiles_n = (static_cast<uint64_t>(N) + 256u * nb - 1) / (256u * nb);
+// block of a 256 x 256 tile at full tensor rate.  Tiles up to 256 wide are
+// bound by the operand bytes each SM pulls from L2 per K block (A 16 KB plus
+// width / 2 B rows of 128 B), so their time follows those bytes rather than
+// the flops: measured on B200, tiles of 224, 192 and 128 columns take 0.95,
+// 0.89 and 0.785 of a 256-wide tile's time (0.875, 0.75 and 0.5 of its
+// flops), fitted as 0.08 + 0.92 x bytes / 32 KB, at 0.85 tensor efficiency
+// for 256.  The 512-wide tile shares one A stage between two MMAs, runs at
+// 0.93 and also pays its non-overlapped epilogue (about 4 K blocks).
+double tile_plan_cost(int width, uint32_t tiles_m, int N, int num_kb, int clusters) {
+  if (clusters <= 0) return 1e300;
+  const uint64_t tiles_n = (static_cast<uint64_t>(N) + width - 1) / width;
   const uint64_t tiles = tiles_m * tiles_n;
   const uint64_t waves = (tiles + clusters - 1) / clusters;
-  const double tile_time = nb == 1 ? num_kb / 0.85 : (2.0 * num_kb + 4.0) / 0.93;
+  double tile_time;
+  if (width == 512) {
+    tile_time = (2.0 * num_kb + 4.0) / 0.93;
+  } else {
+    const double feed = (16384.0 + 64.0 * width) / 32768.0;
+    tile_time = num_kb * (0.08 + 0.92 * feed) / 0.85;
+  }
   return static_cast<double>(waves) * tile_time;
 }
 
@@ -233,9 +261,8 @@ struct b200gemm_handle {
   int device = 0;
   int sm_count = 0;
   int max_clusters = 0;       // co-resident 2-CTA clusters (the smaller of the two instances)
-  int clusters_n256 = 0;      // co-resident clusters of the 256-wide instance
-  int clusters_n512 = 0;      // co-resident clusters of the 512-wide instance
-  int tile_width = 0;         // 0 = choose per call, else 256 or 512
+  int clusters_w[kNumWidths] = {};  // co-resident clusters of each width's instance
+  int tile_width = 0;         // 0 = choose per call, else one of kWidths
   int small_m = -1;           // small-M kernel: -1 or 1 = use it when eligible, 0 = never
   unsigned int* status_dev = nullptr;
   unsigned long long timeout_ns = kDefaultTimeoutNs;
@@ -288,9 +315,12 @@ extern "C" int b200gemm_create(b200gemm_t* out, int device) {
   DeviceGuard guard(device);
   if (!guard.ok()) return B200GEMM_ERR_CUDA;
   if (tensor_map_encoder() == nullptr) return B200GEMM_ERR_CUDA;
-  const int c256 = prepare_kernel<CfgN256>(prop.multiProcessorCount);
-  const int c512 = prepare_kernel<CfgN512>(prop.multiProcessorCount);
-  if (c256 <= 0 || c512 <= 0) return B200GEMM_ERR_CUDA;
+  const int sms = prop.multiProcessorCount;
+  const int cw[kNumWidths] = {prepare_kernel<CfgN256>(sms), prepare_kernel<CfgN512>(sms),
+                              prepare_kernel<CfgN224>(sms), prepare_kernel<CfgN192>(sms),
+                              prepare_kernel<CfgN128>(sms)};
+  for (int i = 0; i < kNumWidths; ++i)
+    if (cw[i] <= 0) return B200GEMM_ERR_CUDA;
   if (!prepare_decode_kernel<DecodeCfg<1>>() || !prepare_decode_kernel<DecodeCfg<2>>() ||
       !prepare_decode_kernel<DecodeCfg<4>>()) {
     return B200GEMM_ERR_CUDA;
@@ -299,9 +329,11 @@ extern "C" int b200gemm_create(b200gemm_t* out, int device) {
   auto* h = new b200gemm_handle();
   h->device = device;
   h->sm_count = prop.multiProcessorCount;
-  h->clusters_n256 = c256;
-  h->clusters_n512 = c512;
-  h->max_clusters = c256 < c512 ? c256 : c512;
+  h->max_clusters = cw[0];
+  for (int i = 0; i < kNumWidths; ++i) {
+    h->clusters_w[i] = cw[i];
+    if (cw[i] < h->max_clusters) h->max_clusters = cw[i];
+  }
   if (cudaMalloc(&h->status_dev, 4 * sizeof(unsigned int)) != cudaSuccess ||
       cudaMemset(h->status_dev, 0, 4 * sizeof(unsigned int)) != cudaSuccess ||
       cudaMalloc(&h->tail_counters, kMaxTailCounters * sizeof(unsigned int)) != cudaSuccess ||
@@ -394,11 +426,11 @@ int schedule_for(b200gemm_t h, uint32_t tiles_m, uint32_t tiles_n, cudaStream_t 
 
 // Tensor maps for one argument tuple, cached in the handle.  Caller holds h->mu.
 int maps_for(b200gemm_t h, int M, int N, int K, const void* A, const void* B, void* C, int ldc,
-             CUtensorMap* ma, CUtensorMap* mb, CUtensorMap* mc) {
+             int b_rows, CUtensorMap* ma, CUtensorMap* mb, CUtensorMap* mc) {
   MapEntry* slot = nullptr;
   for (auto& m : h->maps) {
     if (m.valid && m.a == A && m.b == B && m.c == C && m.M == M && m.N == N && m.K == K &&
-        m.ldc == ldc) {
+        m.ldc == ldc && m.b_rows == b_rows) {
       slot = &m;
       break;
     }
@@ -414,12 +446,13 @@ int maps_for(b200gemm_t h, int M, int N, int K, const void* A, const void* B, vo
     }
     slot->valid = false;
     const uint64_t k = static_cast<uint64_t>(K);
-    // A, B: 64 x 128 boxes (one 128-byte K row per operand row), 128-byte
-    // swizzle as the MMA descriptors expect; C: 32 x 32 boxes, 64-byte swizzle.
+    // A: 64 x 128 boxes, B: 64 x b_rows boxes (one 128-byte K row per operand
+    // row), 128-byte swizzle as the MMA descriptors expect; C: 32 x 32 boxes,
+    // 64-byte swizzle.
     if (!encode_2d(&slot->map_a, A, k, static_cast<uint64_t>(M), k * 2, kBlockK, 128,
                    CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !encode_2d(&slot->map_b, B, k, static_cast<uint64_t>(N), k * 2, kBlockK, 128,
-                   CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_2d(&slot->map_b, B, k, static_cast<uint64_t>(N), k * 2, kBlockK,
+                   static_cast<uint32_t>(b_rows), CU_TENSOR_MAP_SWIZZLE_128B) ||
         !encode_2d(&slot->map_c, C, static_cast<uint64_t>(N), static_cast<uint64_t>(M),
                    static_cast<uint64_t>(ldc) * 2, kCBoxCols, kCBoxRows, CU_TENSOR_MAP_SWIZZLE_64B)) {
       return B200GEMM_ERR_CUDA;
@@ -431,6 +464,7 @@ int maps_for(b200gemm_t h, int M, int N, int K, const void* A, const void* B, vo
     slot->N = N;
     slot->K = K;
     slot->ldc = ldc;
+    slot->b_rows = b_rows;
     slot->valid = true;
   }
   slot->last_use = ++h->tick;
@@ -448,14 +482,36 @@ namespace {
 
 bool tail_split_enabled_for(const b200gemm_handle* h) { return h->tail_split_enabled; }
 
-// Tile width (256 or 512 columns) a call on this handle will use.
+// Tile width (one of kWidths) a call on this handle will use: the cheapest
+// by tile_plan_cost, the earlier entry of kWidths on a tie.
 int choose_tile_width(const b200gemm_handle* h, int M, int N, int K) {
   if (h->tile_width != 0) return h->tile_width;
   const uint32_t tiles_m = static_cast<uint32_t>((M + kTileM - 1) / kTileM);
   const int num_kb = (K + kBlockK - 1) / kBlockK;
-  const double c256 = tile_plan_cost(1, tiles_m, N, num_kb, h->clusters_n256);
-  const double c512 = tile_plan_cost(2, tiles_m, N, num_kb, h->clusters_n512);
-  return c512 < c256 ? 512 : 256;
+  int best = kWidths[0];
+  double best_cost = tile_plan_cost(best, tiles_m, N, num_kb, h->clusters_w[0]);
+  for (int i = 1; i < kNumWidths; ++i) {
+    const double c = tile_plan_cost(kWidths[i], tiles_m, N, num_kb, h->clusters_w[i]);
+    if (c < best_cost) {
+      best_cost = c;
+      best = kWidths[i];
+    }
+  }
+  return best;
+}
+
+// B rows of one CTA's tensor-map box for a tile width.
+int b_box_rows(int width) { return width == 512 ? 128 : width / 2; }
+
+cudaError_t launch_width(int width, int clusters, cudaStream_t stream, const CUtensorMap& ma,
+                         const CUtensorMap& mb, const CUtensorMap& mc, const GemmParams& p) {
+  switch (width) {
+    case 512: return launch_gemm<CfgN512>(clusters, stream, ma, mb, mc, p);
+    case 224: return launch_gemm<CfgN224>(clusters, stream, ma, mb, mc, p);
+    case 192: return launch_gemm<CfgN192>(clusters, stream, ma, mb, mc, p);
+    case 128: return launch_gemm<CfgN128>(clusters, stream, ma, mb, mc, p);
+    default: return launch_gemm<CfgN256>(clusters, stream, ma, mb, mc, p);
+  }
 }
 
 }  // namespace
@@ -598,7 +654,8 @@ int gemm_device(b200gemm_t h, int M, int N, int K, const void* A, const void* B,
   if (ldc < N || (ldc % 8) != 0 || (K % 8) != 0) return B200GEMM_ERR_UNSUPPORTED;
   if (!aligned16(C) || (K > 0 && (!aligned16(A) || !aligned16(B)))) return B200GEMM_ERR_UNSUPPORTED;
   const uint32_t tiles_m = static_cast<uint32_t>((M + kTileM - 1) / kTileM);
-  if (tiles_m > 0xFFFFu || static_cast<uint32_t>((N + kBlockN - 1) / kBlockN) > 0xFFFFu)
+  // Tile coordinates are 16-bit: bound the grid of the narrowest width.
+  if (tiles_m > 0xFFFFu || static_cast<uint32_t>((N + 127) / 128) > 0xFFFFu)
     return B200GEMM_ERR_TOO_LARGE;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
   DeviceGuard guard(h->device);
@@ -632,7 +689,7 @@ int gemm_device(b200gemm_t h, int M, int N, int K, const void* A, const void* B,
     tiles_n = static_cast<uint32_t>((N + width - 1) / width);
     int rc = schedule_for(h, tiles_m, tiles_n, stream, &sched);
     if (rc != B200GEMM_OK) return rc;
-    rc = maps_for(h, M, N, K, A, B, C, ldc, &ma, &mb, &mc);
+    rc = maps_for(h, M, N, K, A, B, C, ldc, b_box_rows(width), &ma, &mb, &mc);
     if (rc != B200GEMM_OK) return rc;
     timeout_ns = h->timeout_ns;
   }
@@ -652,7 +709,7 @@ int gemm_device(b200gemm_t h, int M, int N, int K, const void* A, const void* B,
   for (int i = 0; i < GemmParams::kMaxPeers; ++i)
     p.peer_c[i] = i < npeers ? static_cast<uint8_t*>(peers[i]) : nullptr;
 
-  const int max_clusters = width == 512 ? h->clusters_n512 : h->clusters_n256;
+  const int max_clusters = h->clusters_w[width_index(width)];
   const int clusters = p.num_tiles < max_clusters ? p.num_tiles : max_clusters;
   // Split the last partial wave along K when it leaves clusters idle.
   const int sk = tail_split_enabled_for(h) ? tail_split_for(p.num_tiles, clusters, p.num_kb) : 1;
@@ -690,12 +747,7 @@ int gemm_device(b200gemm_t h, int M, int N, int K, const void* A, const void* B,
     }
   }
 
-  cudaError_t e;
-  if (width == 512) {
-    e = launch_gemm<CfgN512>(clusters, stream, ma, mb, mc, p);
-  } else {
-    e = launch_gemm<CfgN256>(clusters, stream, ma, mb, mc, p);
-  }
+  const cudaError_t e = launch_width(width, clusters, stream, ma, mb, mc, p);
   if (e == cudaSuccess && tail_on) {
     std::lock_guard<std::mutex> lock(h->mu);
     if (cudaEventRecord(h->tail_event, stream) != cudaSuccess) return B200GEMM_ERR_CUDA;
@@ -721,7 +773,7 @@ extern "C" int b200gemm_plan(b200gemm_t h, int M, int N, int K, int* plan) {
   }
   const int width = choose_tile_width(h, M, N, K);
   const int tiles = ((M + kTileM - 1) / kTileM) * ((N + width - 1) / width);
-  const int maxc = width == 512 ? h->clusters_n512 : h->clusters_n256;
+  const int maxc = h->clusters_w[width_index(width)];
   const int clusters = tiles < maxc ? tiles : maxc;
   const int num_kb = (K + kBlockK - 1) / kBlockK;
   plan[0] = 1;  // tiled kernel
@@ -740,7 +792,7 @@ extern "C" int b200gemm_set_tail_split(b200gemm_t h, int enable) {
 }
 
 extern "C" int b200gemm_set_tile_width(b200gemm_t h, int width) {
-  if (h == nullptr || (width != 0 && width != 256 && width != 512)) return B200GEMM_ERR_INVALID_ARG;
+  if (h == nullptr || (width != 0 && width_index(width) < 0)) return B200GEMM_ERR_INVALID_ARG;
   std::lock_guard<std::mutex> lock(h->mu);
   h->tile_width = width;
   return B200GEMM_OK;
@@ -1014,8 +1066,8 @@ extern "C" int b200gemm_bf16_nt_noalloc(int M, int N, int K, const void* A, cons
   }
 
   const int num_kb = (K + kBlockK - 1) / kBlockK;
-  const int width = tile_plan_cost(2, tiles_m, N, num_kb, st.clusters_n512) <
-                            tile_plan_cost(1, tiles_m, N, num_kb, st.clusters_n256)
+  const int width = tile_plan_cost(512, tiles_m, N, num_kb, st.clusters_n512) <
+                            tile_plan_cost(256, tiles_m, N, num_kb, st.clusters_n256)
                         ? 512
                         : 256;
   const uint32_t tiles_n = static_cast<uint32_t>((N + width - 1) / width);

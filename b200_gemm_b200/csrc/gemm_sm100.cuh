@@ -49,7 +49,6 @@ constexpr int kBlockK = 64;       // K per pipeline stage: one 128-byte swizzle 
 constexpr int kMmaK = 16;         // K per tcgen05.mma (kind::f16)
 constexpr int kTmemCols = 512;    // the whole TMEM of the SM
 constexpr int kStageBytesA = 128 * kBlockK * 2;       // A rows of one CTA, one stage
-constexpr int kBlockBytesB = 128 * kBlockK * 2;       // B rows of one CTA for one N block
 constexpr int kCBoxCols = 32;     // one 64-byte row of bf16 (64-byte swizzle)
 constexpr int kCBoxRows = 32;     // one warp's TMEM lane quarter
 constexpr int kCStageBytes = kCBoxCols * kCBoxRows * 2;  // 2 KB staging buffer
@@ -124,13 +123,25 @@ __device__ __forceinline__ WorkUnit unit_at(const GemmParams& p, uint32_t u) {
 //   NB = 2: a pair computes 256 x 512 tiles as two N = 256 MMAs per K step
 //           that share the A stage: 25% fewer operand bytes into each SM per
 //           flop; the single 512-column accumulator is drained by 8 warps.
-template <int STAGES, int NB>
+//   MN (NB = 1 only): columns of one MMA and of the tile, a multiple of 32
+//           up to 256 (e.g. 224 = 1792 / 8 for an N-sharded MLP projection),
+//           so the tile width can divide N and fill the last wave.
+template <int STAGES, int NB, int MN = 256>
 struct GemmCfg {
-  static_assert(NB == 1 || NB == 2, "tile width is 256 or 512 columns");
+  static_assert(NB == 1 || NB == 2, "one or two MMA column blocks per tile");
+  static_assert(MN % 32 == 0 && MN >= 64 && MN <= 256 && (NB == 1 || MN == 256), "MMA width");
   static constexpr int kStages = STAGES;
   static constexpr int kNB = NB;
-  static constexpr int kTileN = kBlockN * NB;
-  static constexpr int kAccBufs = kTmemCols / kTileN;
+  static constexpr int kMmaN = MN;                       // columns per tcgen05.mma
+  static constexpr int kBRows = MN / 2;                  // B rows per CTA per column block
+  static constexpr int kBlockBytesB = kBRows * kBlockK * 2;
+  static constexpr int kChunks = MN / kCBoxCols;         // 32-column epilogue chunks per block
+  static constexpr int kTileN = MN * NB;
+  static constexpr int kAccBufs = NB == 1 ? 2 : 1;
+  static constexpr int kAccStride = 256;                 // TMEM column of accumulator 1
+  // kind::f16: D f32, A = B = bf16, K-major, M = 256 (pair), N = MN.
+  static constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) |
+                                     (static_cast<uint32_t>(MN >> 3) << 17) | ((kTileM >> 4) << 24);
   static constexpr int kEpiWarps = 4 * NB;
   static constexpr int kThreads = 64 + 32 * kEpiWarps;
   static constexpr int kCBufs = 2;   // staging buffers per epilogue warp
@@ -152,13 +163,6 @@ struct GemmCfg {
   static constexpr int kSmemBytes = kEnd + 1024;  // slack to align the base to 1024 B
   static_assert(kSmemBytes <= 232448, "exceeds the 227 KB per-CTA shared memory limit");
 };
-
-// Instruction descriptor, kind::f16: D = f32, A = B = bf16, both K-major,
-// M = 256 (pair), N = 256.
-constexpr uint32_t kIdescBf16 = (1u << 4)            // D format f32
-                                | (1u << 7)          // A format bf16
-                                | (1u << 10)         // B format bf16
-                                | ((kBlockN >> 3) << 17) | ((kTileM >> 4) << 24);
 
 // Shared-memory matrix descriptor fields above the start address for a
 // K-major operand in the 128-byte swizzle layout written by TMA: 8-row groups
@@ -303,7 +307,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
         const uint32_t tile = cur.tile;
         const int row_a = static_cast<int>(tile >> 16) * kTileM + static_cast<int>(rank) * 128;
         const int row_b =
-            static_cast<int>(tile & 0xFFFFu) * Cfg::kTileN + static_cast<int>(rank) * 128;
+            static_cast<int>(tile & 0xFFFFu) * Cfg::kTileN + static_cast<int>(rank) * Cfg::kBRows;
         for (int kb = cur.kb_begin; kb < cur.kb_end; ++kb) {
           if (!ptx::mbar_wait(empty0 + 8 * stage, phase ^ 1u, wd, kSiteProducer, t)) {
             ok = false;
@@ -314,8 +318,8 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
           ptx::tma_load_2d_cg2(sA + stage * kStageBytesA, &map_a, fb, kb * kBlockK, row_a, policy_a);
 #pragma unroll
           for (int h = 0; h < NB; ++h) {
-            ptx::tma_load_2d_cg2(sB + stage * Cfg::kStageBytesB + h * kBlockBytesB, &map_b, fb,
-                                 kb * kBlockK, row_b + h * kBlockN, policy_b);
+            ptx::tma_load_2d_cg2(sB + stage * Cfg::kStageBytesB + h * Cfg::kBlockBytesB, &map_b, fb,
+                                 kb * kBlockK, row_b + h * Cfg::kMmaN, policy_b);
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -336,7 +340,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
         const WorkUnit cur = unit_at(p, t);
         if (!ptx::mbar_wait(tempty0 + 8 * acc, acc_phase ^ 1u, wd, kSiteMmaTmemEmpty, t)) break;
         ptx::tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * Cfg::kTileN;
+        const uint32_t d_tmem = tmem_base + acc * Cfg::kAccStride;
         for (int kb = cur.kb_begin; kb < cur.kb_end; ++kb) {
           if (!ptx::mbar_wait(full0 + 8 * stage, phase, wd, kSiteMmaFull, t)) {
             ok = false;
@@ -351,8 +355,8 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
             for (int h = 0; h < NB; ++h) {
               // +32 bytes per K step inside the 128-byte swizzle row; the
               // second N block of B sits kBlockBytesB further on.
-              ptx::mma_bf16_cg2(d_tmem + h * kBlockN, a_desc + 2 * k,
-                                b_desc + (h * kBlockBytesB >> 4) + 2 * k, kIdescBf16,
+              ptx::mma_bf16_cg2(d_tmem + h * Cfg::kMmaN, a_desc + 2 * k,
+                                b_desc + (h * Cfg::kBlockBytesB >> 4) + 2 * k, Cfg::kIdesc,
                                 (kb > cur.kb_begin || k > 0) ? 1u : 0u);
             }
           }
@@ -401,21 +405,21 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
       ptx::tc_fence_after();
       const int row = static_cast<int>(tile >> 16) * kTileM + static_cast<int>(rank) * 128 +
                       static_cast<int>(quarter) * 32;
-      const int col0 = static_cast<int>(tile & 0xFFFFu) * Cfg::kTileN + static_cast<int>(nblk) * kBlockN;
+      const int col0 = static_cast<int>(tile & 0xFFFFu) * Cfg::kTileN + static_cast<int>(nblk) * Cfg::kMmaN;
       const uint32_t t_row =
-          tmem_base + ((quarter * 32u) << 16) + acc * Cfg::kTileN + nblk * kBlockN;
+          tmem_base + ((quarter * 32u) << 16) + acc * Cfg::kAccStride + nblk * Cfg::kMmaN;
       if (cur.slot < 0 && !live) {
         // nothing to do for this tile
       } else if (cur.slot < 0) {
         // Whole tile: chunks of 32 columns: TMEM -> registers -> bf16 ->
         // swizzled staging buffer -> TMA store, two buffers in flight per warp.
 #pragma unroll 1
-        for (int c = 0; c < kBlockN / kCBoxCols; ++c) {
+        for (int c = 0; c < Cfg::kChunks; ++c) {
           uint32_t v[32];
           ptx::tmem_ld_32x32b_x32(t_row + c * kCBoxCols, v);
           ptx::tmem_wait_ld();
           ptx::reg_fence32(v);
-          if (c == kBlockN / kCBoxCols - 1) {
+          if (c == Cfg::kChunks - 1) {
             // This warp's part of the accumulator is in registers: release it.
             ptx::tc_fence_before();
             __syncwarp();
@@ -436,14 +440,14 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
         auto part = [&](int slot) { return p.workspace + (static_cast<size_t>(slot) * 2 + rank) * slab; };
         float* mine = part(cur.slot);
 #pragma unroll 1
-        for (int c = 0; c < (live ? kBlockN / kCBoxCols : 0); ++c) {
+        for (int c = 0; c < (live ? Cfg::kChunks : 0); ++c) {
           uint32_t v[32];
           ptx::tmem_ld_32x32b_x32(t_row + c * kCBoxCols, v);
           ptx::tmem_wait_ld();
           ptx::reg_fence32(v);
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            const size_t g = static_cast<size_t>((nblk * (kBlockN / kCBoxCols) + c) * 8 + j);
+            const size_t g = static_cast<size_t>((nblk * (Cfg::kChunks) + c) * 8 + j);
             ptx::st_global_v4(mine + (g * 128 + i) * 4, v[4 * j], v[4 * j + 1], v[4 * j + 2],
                               v[4 * j + 3]);
           }
@@ -467,7 +471,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
           __threadfence();
           const int first = tile_r * p.tail_split;
 #pragma unroll 1
-          for (int c = 0; c < kBlockN / kCBoxCols; ++c) {
+          for (int c = 0; c < Cfg::kChunks; ++c) {
             // Sum the slices in slice order whichever slice arrives last, so
             // the result does not depend on timing; this slice's own partial
             // comes from TMEM at its place in the order.  Two 16-column halves
@@ -491,7 +495,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
 #pragma unroll
                   for (int j = 0; j < 4; ++j) {
                     const size_t g =
-                        static_cast<size_t>((nblk * (kBlockN / kCBoxCols) + c) * 8 + hh * 4 + j);
+                        static_cast<size_t>((nblk * (Cfg::kChunks) + c) * 8 + hh * 4 + j);
                     uint32_t x0, x1, x2, x3;
                     ptx::ld_global_cg_v4(other + (g * 128 + i) * 4, x0, x1, x2, x3);
                     x[4 * j] = __uint_as_float(x0);

@@ -58,7 +58,7 @@ def parse_args(argv=None):
     p.add_argument("--impl", default="ours", choices=["ours", "reference", "cublaslt"],
                    help="ours: this library; reference: the reference arithmetic on the host CPU; "
                         "cublaslt: torch.matmul with the cuBLASLt backend on the same operands")
-    p.add_argument("--tile-width", type=int, default=0, choices=[0, 256, 512],
+    p.add_argument("--tile-width", type=int, default=0, choices=[0, 512, 256, 224, 192, 128],
                    help="force the output tile width (0 = the library's per-shape choice)")
     p.add_argument("--order", default="default", choices=["default", "hilbert", "bands"])
     p.add_argument("--band", type=int, default=16, help="tile-rows per band for --order bands")

@@ -123,8 +123,11 @@ int b200gemm_device_info(b200gemm_t handle, int* sm_count, int* max_clusters);
 /* Output tile width of the handle's GEMM calls: 256 (256 x 256 tiles, two
  * TMEM accumulators so a tile's epilogue overlaps the next tile's MMAs), 512
  * (256 x 512 tiles: one A stage feeds two MMAs, a quarter less operand
- * traffic per flop), or 0 (default) to choose per call from the shape.
- * The reference has one fixed 256 x 256 configuration (matmul_1.cuh:13-22). */
+ * traffic per flop), 224, 192 or 128 (narrower 256-row tiles, for N that
+ * wider tiles split into a partly idle last wave, e.g. N = 1792 = 8 x 224),
+ * or 0 (default) to choose per call from the shape.  Any other value is
+ * B200GEMM_ERR_INVALID_ARG.  The reference has one fixed 256 x 256
+ * configuration (matmul_1.cuh:13-22). */
 int b200gemm_set_tile_width(b200gemm_t handle, int width);
 
 /* Split the last, partial wave of tiles along K (default off): when T tiles
@@ -140,8 +143,8 @@ int b200gemm_set_tail_split(b200gemm_t handle, int enable);
  * last partial wave (1 = none; tiled kernel), K split of the small-M kernel. */
 int b200gemm_plan(b200gemm_t handle, int M, int N, int K, int* plan);
 
-/* The tile width (256 or 512) a call with this shape would use now; 0 for
- * an invalid handle or shape. */
+/* The tile width (512, 256, 224, 192 or 128) a call with this shape would
+ * use now; 0 for an invalid handle or shape. */
 int b200gemm_tile_width_for(b200gemm_t handle, int M, int N, int K);
 
 /* Small-M kernel (M <= 128, N % 8 == 0, K >= 128): rows of B become the MMA's

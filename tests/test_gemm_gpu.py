@@ -65,7 +65,10 @@ SHAPES = [
 ]
 
 
-@pytest.fixture(params=[256, 512], ids=["w256", "w512"])
+WIDTHS = [256, 512, 224, 192, 128]
+
+
+@pytest.fixture(params=WIDTHS, ids=[f"w{w}" for w in WIDTHS])
 def width_handle(request, gpu_handle):
     """The session handle forced to one tile width for the test."""
     gpu_handle.set_tile_width(request.param)
@@ -130,13 +133,18 @@ def test_k_zero_writes_zeros(gpu_handle):
 
 def test_tile_width_selection(gpu_handle):
     h = gpu_handle
-    assert h.tile_width_for(8192, 8192, 8192) in (256, 512)
-    assert h.tile_width_for(256, 256, 64) == 256  # one tile: the narrow tile wastes nothing
-    h.set_tile_width(512)
-    assert h.tile_width_for(256, 256, 64) == 512
+    assert h.tile_width_for(8192, 8192, 8192) == 512
+    assert h.tile_width_for(256, 256, 64) in WIDTHS
+    # N-sharded MLP projection: 1792 = 8 x 224 columns fill the last wave
+    assert h.tile_width_for(16384, 1792, 4096) == 224
+    for w in WIDTHS:
+        h.set_tile_width(w)
+        assert h.tile_width_for(256, 256, 64) == w
+        assert h.plan(512, 1792, 256)["tile_width"] == w
     h.set_tile_width(0)
-    with pytest.raises(Exception):
-        h.set_tile_width(384)
+    for bad in (384, 64, 96, -1):
+        with pytest.raises(Exception):
+            h.set_tile_width(bad)
 
 
 def test_device_info(gpu_handle):
@@ -236,9 +244,10 @@ def test_8192_vs_cublaslt_and_sampled_oracle(gpu_handle, oracle_mod):
     assert oracle_mod.within_tolerance(got, ref).all()
 
 
-@pytest.mark.parametrize("width", [256, 512])
+@pytest.mark.parametrize("width", WIDTHS[1:])
 def test_8192_widths_agree(gpu_handle, width):
-    """Both tile widths give bit-identical results (same per-element K order)."""
+    """Every tile width gives the 256-wide result bit for bit (same per-element
+    K order)."""
     M = N = K = 8192
     A, B = data.device_operands(M, N, K, "normal", seed=4)
     gpu_handle.set_tile_width(256)
