@@ -25,6 +25,10 @@ def version() -> int:
     return _lib.load().b200gemm_version()
 
 
+_ACTIVATIONS = {"none": _lib.ACT_NONE, "relu": _lib.ACT_RELU, "gelu": _lib.ACT_GELU,
+                "gelu_tanh": _lib.ACT_GELU_TANH, "silu": _lib.ACT_SILU}
+
+
 def _ptr(t) -> int:
     return 0 if t is None else int(t.data_ptr())
 
@@ -99,6 +103,55 @@ class Gemm:
         ldc = out.stride(0) if M > 1 else 8 * ((N + 7) // 8)
         rc = self.bf16_nt_ptr(M, N, K, _ptr(A), _ptr(B), _ptr(out), ldc, _stream_ptr(stream))
         _lib.check(rc, "b200gemm_bf16_nt")
+        return out
+
+    def bf16_nt_epilogue(self, A, B, bias=None, activation: str = "none", residual=None,
+                         alpha: float = 1.0, beta: float = 1.0, out=None, out_dtype=None,
+                         stream=None):
+        """out = act(alpha * A @ B^T + bias) + beta * residual, fused into the
+        GEMM's epilogue (fp32 math, one pass over C).
+
+        bias: bf16 [N] CUDA tensor or None; residual: bf16 [M, N] row-major
+        view (row stride = ldr) or None; activation: none, relu, gelu,
+        gelu_tanh, silu; out_dtype: torch.bfloat16 (default) or torch.float32.
+        """
+        import torch
+
+        if A.dtype != torch.bfloat16 or B.dtype != torch.bfloat16:
+            raise TypeError("A and B must be torch.bfloat16")
+        if A.dim() != 2 or B.dim() != 2 or A.shape[1] != B.shape[1]:
+            raise ValueError(f"shape mismatch: A {tuple(A.shape)}, B {tuple(B.shape)}")
+        if A.stride(1) != 1 or B.stride(1) != 1 or A.stride(0) != A.shape[1] or B.stride(0) != B.shape[1]:
+            raise ValueError("A and B must be contiguous row-major (K-major)")
+        if activation not in _ACTIVATIONS:
+            raise ValueError(f"activation must be one of {sorted(_ACTIVATIONS)}")
+        M, K = A.shape
+        N = B.shape[0]
+        if out_dtype is None:
+            out_dtype = out.dtype if out is not None else torch.bfloat16
+        if out_dtype not in (torch.bfloat16, torch.float32):
+            raise TypeError("out_dtype must be torch.bfloat16 or torch.float32")
+        group = 8 if out_dtype == torch.bfloat16 else 4  # elements per 16 bytes
+        if out is None:
+            pitch = group * ((N + group - 1) // group)
+            out = torch.empty(M, pitch, device=A.device, dtype=out_dtype)[:, :N]
+        if out.dtype != out_dtype or tuple(out.shape) != (M, N) or out.stride(1) != 1:
+            raise ValueError("out must be an [M, N] row-major view of out_dtype")
+        ldc = out.stride(0) if M > 1 else group * ((N + group - 1) // group)
+        epi = _lib.Epilogue(alpha=float(alpha), beta=float(beta), activation=_ACTIVATIONS[activation],
+                            out_type=_lib.OUT_F32 if out_dtype == torch.float32 else _lib.OUT_BF16)
+        if bias is not None:
+            if bias.dtype != torch.bfloat16 or tuple(bias.shape) != (N,) or bias.stride(0) != 1:
+                raise ValueError("bias must be a contiguous bf16 [N] tensor")
+            epi.bias = _ptr(bias)
+        if residual is not None:
+            if residual.dtype != torch.bfloat16 or tuple(residual.shape) != (M, N) or residual.stride(1) != 1:
+                raise ValueError("residual must be a bf16 [M, N] row-major view")
+            epi.residual = _ptr(residual)
+            epi.ldr = residual.stride(0) if M > 1 else 8 * ((N + 7) // 8)
+        rc = self._lib.b200gemm_bf16_nt_epilogue(self._h, M, N, K, _ptr(A), _ptr(B), _ptr(out), ldc,
+                                                 ctypes.byref(epi), _stream_ptr(stream))
+        _lib.check(rc, "b200gemm_bf16_nt_epilogue")
         return out
 
     def bf16_nt_host(self, A, B, out=None, stream=None):

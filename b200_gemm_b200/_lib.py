@@ -23,7 +23,25 @@ ERR_TOO_LARGE = 6
 ORDER_HILBERT = 0
 ORDER_BANDS = 1
 
+ACT_NONE, ACT_RELU, ACT_GELU, ACT_GELU_TANH, ACT_SILU = 0, 1, 2, 3, 4
+OUT_BF16, OUT_F32 = 0, 1
+
 _c_int, _c_uint, _c_ull, _vp = ctypes.c_int, ctypes.c_uint, ctypes.c_ulonglong, ctypes.c_void_p
+
+
+class Epilogue(ctypes.Structure):
+    """struct b200gemm_epilogue (include/b200gemm.h)."""
+    _fields_ = [
+        ("alpha", ctypes.c_float),
+        ("beta", ctypes.c_float),
+        ("bias", _vp),
+        ("residual", _vp),
+        ("ldr", _c_int),
+        ("activation", _c_int),
+        ("out_type", _c_int),
+        ("reserved", _c_int),
+    ]
+
 
 # name -> (restype, argtypes); one line per declaration in include/b200gemm.h
 SIGNATURES = {
@@ -31,6 +49,8 @@ SIGNATURES = {
     "b200gemm_destroy": (None, [_vp]),
     "b200gemm_bf16_nt": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp, _vp, _vp, _c_int, _vp]),
     "b200gemm_bf16_nt_host": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp, _vp, _vp, _c_int, _vp]),
+    "b200gemm_bf16_nt_epilogue": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp, _vp, _vp, _c_int,
+                                           ctypes.POINTER(Epilogue), _vp]),
     "b200gemm_bf16_nt_allgather": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp, _vp, _vp, _c_int,
                                             ctypes.POINTER(_vp), _c_int, _vp]),
     "b200gemm_ipc_get_handle": (_c_int, [_vp, _vp, ctypes.POINTER(_c_ull)]),

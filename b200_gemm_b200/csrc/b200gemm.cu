@@ -39,6 +39,12 @@ using CfgN512 = GemmCfg<B200GEMM_STAGES_N512, 2>;  // 256 x 512 tiles, shared A 
 using CfgN224 = GemmCfg<6, 1, 224>;
 using CfgN192 = GemmCfg<7, 1, 192>;
 using CfgN128 = GemmCfg<8, 1, 128>;
+// The same five widths with the fused epilogue compiled in.
+using CfgE256 = GemmCfg<B200GEMM_STAGES_N256, 1, 256, true>;
+using CfgE512 = GemmCfg<B200GEMM_STAGES_N512, 2, 256, true>;
+using CfgE224 = GemmCfg<6, 1, 224, true>;
+using CfgE192 = GemmCfg<7, 1, 192, true>;
+using CfgE128 = GemmCfg<8, 1, 128, true>;
 // Tile widths of the tiled kernel, in the order the cost model prefers them
 // on a tie; index i of every per-width table below.
 constexpr int kWidths[] = {256, 512, 224, 192, 128};
@@ -108,11 +114,12 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-// Row-major bf16 matrix [outer x inner] with a row pitch in bytes, read or
+// Row-major matrix [outer x inner] (bf16 unless `dtype` says otherwise) with a row pitch in bytes, read or
 // written in boxes of [box_outer x box_inner] through a shared-memory swizzle.
 bool encode_2d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer,
                uint64_t pitch_bytes, uint32_t box_inner, uint32_t box_outer,
-               CUtensorMapSwizzle swizzle) {
+               CUtensorMapSwizzle swizzle,
+               CUtensorMapDataType dtype = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16) {
   auto encode = tensor_map_encoder();
   if (encode == nullptr) return false;
   cuuint64_t dims[2] = {inner, outer};
@@ -120,7 +127,7 @@ bool encode_2d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t elem_strides[2] = {1, 1};
   const CUresult r =
-      encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box,
+      encode(map, dtype, 2, const_cast<void*>(ptr), dims, strides, box,
              elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
@@ -133,6 +140,7 @@ struct MapEntry {
   void* c = nullptr;
   int M = 0, N = 0, K = 0, ldc = 0;
   int b_rows = 0;   // rows of B's box: B rows one CTA loads per MMA column block
+  bool c_f32 = false;  // C holds fp32 (fused epilogue output type)
   uint64_t last_use = 0;
   CUtensorMap map_a, map_b, map_c;
 };
@@ -222,21 +230,55 @@ cudaError_t launch_gemm(int clusters, cudaStream_t stream, const CUtensorMap& ma
 // the flops: measured on B200, tiles of 224, 192 and 128 columns take 0.95,
 // 0.89 and 0.785 of a 256-wide tile's time (0.875, 0.75 and 0.5 of its
 // flops), fitted as 0.08 + 0.92 x bytes / 32 KB, at 0.85 tensor efficiency
-// for 256.  The 512-wide tile shares one A stage between two MMAs, runs at
-// 0.93 and also pays its non-overlapped epilogue (about 4 K blocks).
-double tile_plan_cost(int width, uint32_t tiles_m, int N, int num_kb, int clusters) {
+// for 256.  The 512-wide tile shares one A stage between two MMAs and pays
+// its non-overlapped epilogue; fitted on 8192^3 and 16384 x 14336 x 4096
+// (where 512 wins by 9.8% and 1.3%): its K blocks run 1 / 0.8545 as fast
+// per flop as the 256-wide tile's and the epilogue costs 17 K blocks.
+// `epi` adds the fused epilogue's measured per-tile cost (epilogue_cost).
+double tile_plan_cost(int width, uint32_t tiles_m, int N, int num_kb, int clusters,
+                      double epi = 0.0) {
   if (clusters <= 0) return 1e300;
   const uint64_t tiles_n = (static_cast<uint64_t>(N) + width - 1) / width;
   const uint64_t tiles = tiles_m * tiles_n;
   const uint64_t waves = (tiles + clusters - 1) / clusters;
   double tile_time;
   if (width == 512) {
-    tile_time = (2.0 * num_kb + 4.0) / 0.93;
+    tile_time = (2.0 * num_kb + 17.0) * 0.8545 / 0.85;
   } else {
     const double feed = (16384.0 + 64.0 * width) / 32768.0;
     tile_time = num_kb * (0.08 + 0.92 * feed) / 0.85;
   }
-  return static_cast<double>(waves) * tile_time;
+  return static_cast<double>(waves) * (tile_time + epi);
+}
+
+// Per-tile cost of a fused epilogue, in tile_plan_cost's units, measured on
+// B200 at 8192^3 and 16384 x 14336 x 4096 (constant in K): the 512-wide
+// tile pays it in full (its epilogue is not overlapped with MMAs), a 256-wide
+// tile about a third (its epilogue overlaps the next tile's MMAs), narrower
+// tiles in proportion to their columns.
+double epilogue_cost(const b200gemm_epilogue* epi, int width) {
+  if (epi == nullptr) return 0.0;
+  double w512 = 0.0, w256 = 0.0;
+  switch (epi->activation) {
+    case B200GEMM_ACT_RELU: w512 = 8.0; w256 = 2.5; break;
+    case B200GEMM_ACT_GELU_TANH: w512 = 14.0; w256 = 5.0; break;
+    case B200GEMM_ACT_GELU: w512 = 28.0; w256 = 10.0; break;
+    case B200GEMM_ACT_SILU: w512 = 16.0; w256 = 4.6; break;
+    default: break;
+  }
+  if (epi->residual != nullptr) {
+    w512 += 16.0;
+    w256 += 6.0;
+  }
+  if (epi->bias != nullptr && epi->activation == B200GEMM_ACT_NONE && epi->residual == nullptr) {
+    w512 += 6.0;
+    w256 += 2.2;
+  }
+  if (epi->out_type == B200GEMM_OUT_F32) {
+    w512 += 12.0;
+    w256 += 4.0;
+  }
+  return width == 512 ? w512 : w256 * width / 256.0;
 }
 
 }  // namespace b200gemm
@@ -262,6 +304,7 @@ struct b200gemm_handle {
   int sm_count = 0;
   int max_clusters = 0;       // co-resident 2-CTA clusters (the smaller of the two instances)
   int clusters_w[kNumWidths] = {};  // co-resident clusters of each width's instance
+  int clusters_epi[kNumWidths] = {};  // the same for the fused-epilogue instances
   int tile_width = 0;         // 0 = choose per call, else one of kWidths
   int small_m = -1;           // small-M kernel: -1 or 1 = use it when eligible, 0 = never
   unsigned int* status_dev = nullptr;
@@ -319,8 +362,11 @@ extern "C" int b200gemm_create(b200gemm_t* out, int device) {
   const int cw[kNumWidths] = {prepare_kernel<CfgN256>(sms), prepare_kernel<CfgN512>(sms),
                               prepare_kernel<CfgN224>(sms), prepare_kernel<CfgN192>(sms),
                               prepare_kernel<CfgN128>(sms)};
+  const int ce[kNumWidths] = {prepare_kernel<CfgE256>(sms), prepare_kernel<CfgE512>(sms),
+                              prepare_kernel<CfgE224>(sms), prepare_kernel<CfgE192>(sms),
+                              prepare_kernel<CfgE128>(sms)};
   for (int i = 0; i < kNumWidths; ++i)
-    if (cw[i] <= 0) return B200GEMM_ERR_CUDA;
+    if (cw[i] <= 0 || ce[i] <= 0) return B200GEMM_ERR_CUDA;
   if (!prepare_decode_kernel<DecodeCfg<1>>() || !prepare_decode_kernel<DecodeCfg<2>>() ||
       !prepare_decode_kernel<DecodeCfg<4>>()) {
     return B200GEMM_ERR_CUDA;
@@ -332,6 +378,7 @@ extern "C" int b200gemm_create(b200gemm_t* out, int device) {
   h->max_clusters = cw[0];
   for (int i = 0; i < kNumWidths; ++i) {
     h->clusters_w[i] = cw[i];
+    h->clusters_epi[i] = ce[i];
     if (cw[i] < h->max_clusters) h->max_clusters = cw[i];
   }
   if (cudaMalloc(&h->status_dev, 4 * sizeof(unsigned int)) != cudaSuccess ||
@@ -426,11 +473,11 @@ int schedule_for(b200gemm_t h, uint32_t tiles_m, uint32_t tiles_n, cudaStream_t 
 
 // Tensor maps for one argument tuple, cached in the handle.  Caller holds h->mu.
 int maps_for(b200gemm_t h, int M, int N, int K, const void* A, const void* B, void* C, int ldc,
-             int b_rows, CUtensorMap* ma, CUtensorMap* mb, CUtensorMap* mc) {
+             int b_rows, bool c_f32, CUtensorMap* ma, CUtensorMap* mb, CUtensorMap* mc) {
   MapEntry* slot = nullptr;
   for (auto& m : h->maps) {
     if (m.valid && m.a == A && m.b == B && m.c == C && m.M == M && m.N == N && m.K == K &&
-        m.ldc == ldc && m.b_rows == b_rows) {
+        m.ldc == ldc && m.b_rows == b_rows && m.c_f32 == c_f32) {
       slot = &m;
       break;
     }
@@ -447,14 +494,16 @@ int maps_for(b200gemm_t h, int M, int N, int K, const void* A, const void* B, vo
     slot->valid = false;
     const uint64_t k = static_cast<uint64_t>(K);
     // A: 64 x 128 boxes, B: 64 x b_rows boxes (one 128-byte K row per operand
-    // row), 128-byte swizzle as the MMA descriptors expect; C: 32 x 32 boxes,
-    // 64-byte swizzle.
+    // row), 128-byte swizzle as the MMA descriptors expect; C: 32 rows of 64
+    // bytes (32 bf16 or 16 fp32 columns), 64-byte swizzle.
     if (!encode_2d(&slot->map_a, A, k, static_cast<uint64_t>(M), k * 2, kBlockK, 128,
                    CU_TENSOR_MAP_SWIZZLE_128B) ||
         !encode_2d(&slot->map_b, B, k, static_cast<uint64_t>(N), k * 2, kBlockK,
                    static_cast<uint32_t>(b_rows), CU_TENSOR_MAP_SWIZZLE_128B) ||
         !encode_2d(&slot->map_c, C, static_cast<uint64_t>(N), static_cast<uint64_t>(M),
-                   static_cast<uint64_t>(ldc) * 2, kCBoxCols, kCBoxRows, CU_TENSOR_MAP_SWIZZLE_64B)) {
+                   static_cast<uint64_t>(ldc) * (c_f32 ? 4 : 2), c_f32 ? kCBoxCols / 2 : kCBoxCols,
+                   kCBoxRows, CU_TENSOR_MAP_SWIZZLE_64B,
+                   c_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16)) {
       return B200GEMM_ERR_CUDA;
     }
     slot->a = A;
@@ -465,6 +514,7 @@ int maps_for(b200gemm_t h, int M, int N, int K, const void* A, const void* B, vo
     slot->K = K;
     slot->ldc = ldc;
     slot->b_rows = b_rows;
+    slot->c_f32 = c_f32;
     slot->valid = true;
   }
   slot->last_use = ++h->tick;
@@ -483,15 +533,19 @@ namespace {
 bool tail_split_enabled_for(const b200gemm_handle* h) { return h->tail_split_enabled; }
 
 // Tile width (one of kWidths) a call on this handle will use: the cheapest
-// by tile_plan_cost, the earlier entry of kWidths on a tie.
-int choose_tile_width(const b200gemm_handle* h, int M, int N, int K) {
+// by tile_plan_cost (with the fused epilogue's cost when `epi` is given), the
+// earlier entry of kWidths on a tie.
+int choose_tile_width(const b200gemm_handle* h, int M, int N, int K,
+                      const b200gemm_epilogue* epi = nullptr) {
   if (h->tile_width != 0) return h->tile_width;
   const uint32_t tiles_m = static_cast<uint32_t>((M + kTileM - 1) / kTileM);
   const int num_kb = (K + kBlockK - 1) / kBlockK;
+  const int* clusters = epi != nullptr ? h->clusters_epi : h->clusters_w;
   int best = kWidths[0];
-  double best_cost = tile_plan_cost(best, tiles_m, N, num_kb, h->clusters_w[0]);
+  double best_cost = tile_plan_cost(best, tiles_m, N, num_kb, clusters[0], epilogue_cost(epi, best));
   for (int i = 1; i < kNumWidths; ++i) {
-    const double c = tile_plan_cost(kWidths[i], tiles_m, N, num_kb, h->clusters_w[i]);
+    const double c = tile_plan_cost(kWidths[i], tiles_m, N, num_kb, clusters[i],
+                                    epilogue_cost(epi, kWidths[i]));
     if (c < best_cost) {
       best_cost = c;
       best = kWidths[i];
@@ -503,8 +557,18 @@ int choose_tile_width(const b200gemm_handle* h, int M, int N, int K) {
 // B rows of one CTA's tensor-map box for a tile width.
 int b_box_rows(int width) { return width == 512 ? 128 : width / 2; }
 
-cudaError_t launch_width(int width, int clusters, cudaStream_t stream, const CUtensorMap& ma,
-                         const CUtensorMap& mb, const CUtensorMap& mc, const GemmParams& p) {
+cudaError_t launch_width(int width, bool fused, int clusters, cudaStream_t stream,
+                         const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc,
+                         const GemmParams& p) {
+  if (fused) {
+    switch (width) {
+      case 512: return launch_gemm<CfgE512>(clusters, stream, ma, mb, mc, p);
+      case 224: return launch_gemm<CfgE224>(clusters, stream, ma, mb, mc, p);
+      case 192: return launch_gemm<CfgE192>(clusters, stream, ma, mb, mc, p);
+      case 128: return launch_gemm<CfgE128>(clusters, stream, ma, mb, mc, p);
+      default: return launch_gemm<CfgE256>(clusters, stream, ma, mb, mc, p);
+    }
+  }
   switch (width) {
     case 512: return launch_gemm<CfgN512>(clusters, stream, ma, mb, mc, p);
     case 224: return launch_gemm<CfgN224>(clusters, stream, ma, mb, mc, p);
@@ -576,12 +640,19 @@ extern "C" int b200gemm_set_small_m(b200gemm_t h, int mode) {
 namespace {
 int gemm_device(b200gemm_t h, int M, int N, int K, const void* A, const void* B, void* C, int ldc,
                 void* stream_ptr, bool allow_small_m, int npeers = 0,
-                void* const* peers = nullptr);
+                void* const* peers = nullptr, const b200gemm_epilogue* epi = nullptr);
 }  // namespace
 
 extern "C" int b200gemm_bf16_nt(b200gemm_t h, int M, int N, int K, const void* A, const void* B,
                                 void* C, int ldc, void* stream_ptr) {
   return gemm_device(h, M, N, K, A, B, C, ldc, stream_ptr, true);
+}
+
+extern "C" int b200gemm_bf16_nt_epilogue(b200gemm_t h, int M, int N, int K, const void* A,
+                                         const void* B, void* C, int ldc,
+                                         const b200gemm_epilogue* epi, void* stream_ptr) {
+  if (epi == nullptr) return gemm_device(h, M, N, K, A, B, C, ldc, stream_ptr, true);
+  return gemm_device(h, M, N, K, A, B, C, ldc, stream_ptr, /*allow_small_m=*/false, 0, nullptr, epi);
 }
 
 extern "C" int b200gemm_bf16_nt_allgather(b200gemm_t h, int M, int N, int K, const void* A,
@@ -647,11 +718,24 @@ namespace {
 // chunking never changes which kernel, and hence which summation order, an
 // element gets).
 int gemm_device(b200gemm_t h, int M, int N, int K, const void* A, const void* B, void* C, int ldc,
-                void* stream_ptr, bool allow_small_m, int npeers, void* const* peers) {
+                void* stream_ptr, bool allow_small_m, int npeers, void* const* peers,
+                const b200gemm_epilogue* epi) {
   if (h == nullptr || M < 0 || N < 0 || K < 0) return B200GEMM_ERR_INVALID_ARG;
+  const bool fused = epi != nullptr;
+  const bool c_f32 = fused && epi->out_type == B200GEMM_OUT_F32;
+  if (fused) {
+    if (epi->out_type != B200GEMM_OUT_BF16 && epi->out_type != B200GEMM_OUT_F32)
+      return B200GEMM_ERR_INVALID_ARG;
+    if (epi->activation < B200GEMM_ACT_NONE || epi->activation > B200GEMM_ACT_SILU)
+      return B200GEMM_ERR_INVALID_ARG;
+    if (epi->residual != nullptr && (epi->ldr < N || (epi->ldr % 8) != 0 || !aligned16(epi->residual)))
+      return B200GEMM_ERR_UNSUPPORTED;
+    if (epi->bias != nullptr && !aligned16(epi->bias)) return B200GEMM_ERR_UNSUPPORTED;
+  }
   if (M == 0 || N == 0) return B200GEMM_OK;
   if (C == nullptr || (K > 0 && (A == nullptr || B == nullptr))) return B200GEMM_ERR_INVALID_ARG;
-  if (ldc < N || (ldc % 8) != 0 || (K % 8) != 0) return B200GEMM_ERR_UNSUPPORTED;
+  if (ldc < N || (ldc % (c_f32 ? 4 : 8)) != 0 || (K % 8) != 0) return B200GEMM_ERR_UNSUPPORTED;
+  if (fused && K == 0) return B200GEMM_ERR_UNSUPPORTED;  // the kernel needs one K block
   if (!aligned16(C) || (K > 0 && (!aligned16(A) || !aligned16(B)))) return B200GEMM_ERR_UNSUPPORTED;
   const uint32_t tiles_m = static_cast<uint32_t>((M + kTileM - 1) / kTileM);
   // Tile coordinates are 16-bit: bound the grid of the narrowest width.
@@ -673,7 +757,7 @@ int gemm_device(b200gemm_t h, int M, int N, int K, const void* A, const void* B,
   unsigned long long decode_timeout;
   {
     std::lock_guard<std::mutex> lock(h->mu);
-    split = (allow_small_m && h->small_m != 0) ? decode_split(M, N, K, h->sm_count) : 0;
+    split = (allow_small_m && !fused && h->small_m != 0) ? decode_split(M, N, K, h->sm_count) : 0;
     decode_timeout = h->timeout_ns;
   }
   if (split > 0) return run_decode(h, split, M, N, K, A, B, C, ldc, stream, decode_timeout);
@@ -685,16 +769,16 @@ int gemm_device(b200gemm_t h, int M, int N, int K, const void* A, const void* B,
   uint32_t tiles_n;
   {
     std::lock_guard<std::mutex> lock(h->mu);
-    width = choose_tile_width(h, M, N, K);
+    width = choose_tile_width(h, M, N, K, epi);
     tiles_n = static_cast<uint32_t>((N + width - 1) / width);
     int rc = schedule_for(h, tiles_m, tiles_n, stream, &sched);
     if (rc != B200GEMM_OK) return rc;
-    rc = maps_for(h, M, N, K, A, B, C, ldc, b_box_rows(width), &ma, &mb, &mc);
+    rc = maps_for(h, M, N, K, A, B, C, ldc, b_box_rows(width), c_f32, &ma, &mb, &mc);
     if (rc != B200GEMM_OK) return rc;
     timeout_ns = h->timeout_ns;
   }
 
-  GemmParams p;
+  GemmParams p{};
   p.M = M;
   p.N = N;
   p.K = K;
@@ -709,10 +793,29 @@ int gemm_device(b200gemm_t h, int M, int N, int K, const void* A, const void* B,
   for (int i = 0; i < GemmParams::kMaxPeers; ++i)
     p.peer_c[i] = i < npeers ? static_cast<uint8_t*>(peers[i]) : nullptr;
 
-  const int max_clusters = h->clusters_w[width_index(width)];
+  p.epi_flags = 0;
+  p.act = B200GEMM_ACT_NONE;
+  p.out_f32 = c_f32 ? 1 : 0;
+  p.alpha = 1.0f;
+  p.beta = 0.0f;
+  p.bias = nullptr;
+  p.residual = nullptr;
+  p.ldr = 0;
+  if (fused) {
+    p.epi_flags = (epi->bias != nullptr ? kEpiBias : 0u) | (epi->residual != nullptr ? kEpiResidual : 0u);
+    p.act = epi->activation;
+    p.alpha = epi->alpha;
+    p.beta = epi->beta;
+    p.bias = static_cast<const uint16_t*>(epi->bias);
+    p.residual = static_cast<const uint16_t*>(epi->residual);
+    p.ldr = epi->ldr;
+  }
+
+  const int max_clusters = fused ? h->clusters_epi[width_index(width)] : h->clusters_w[width_index(width)];
   const int clusters = p.num_tiles < max_clusters ? p.num_tiles : max_clusters;
-  // Split the last partial wave along K when it leaves clusters idle.
-  const int sk = tail_split_enabled_for(h) ? tail_split_for(p.num_tiles, clusters, p.num_kb) : 1;
+  // Split the last partial wave along K when it leaves clusters idle (plain
+  // epilogue only: the split tiles' reduction writes bf16 directly).
+  const int sk = (tail_split_enabled_for(h) && !fused) ? tail_split_for(p.num_tiles, clusters, p.num_kb) : 1;
   p.tail_start = p.num_tiles;
   p.tail_split = 1;
   p.tail_kb = p.num_kb;
@@ -747,7 +850,7 @@ int gemm_device(b200gemm_t h, int M, int N, int K, const void* A, const void* B,
     }
   }
 
-  const cudaError_t e = launch_width(width, clusters, stream, ma, mb, mc, p);
+  const cudaError_t e = launch_width(width, fused, clusters, stream, ma, mb, mc, p);
   if (e == cudaSuccess && tail_on) {
     std::lock_guard<std::mutex> lock(h->mu);
     if (cudaEventRecord(h->tail_event, stream) != cudaSuccess) return B200GEMM_ERR_CUDA;
@@ -1092,7 +1195,7 @@ extern "C" int b200gemm_bf16_nt_noalloc(int M, int N, int K, const void* A, cons
                                                 B200GEMM_DEFAULT_BAND, table);
   if (cudaGetLastError() != cudaSuccess) return B200GEMM_ERR_CUDA;
 
-  GemmParams p;
+  GemmParams p{};
   p.M = M;
   p.N = N;
   p.K = K;

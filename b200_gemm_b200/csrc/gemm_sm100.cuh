@@ -89,7 +89,21 @@ struct GemmParams {
   int tail_kb;
   float* workspace;     // [tail unit][CTA of the pair][128 rows x tile width] fp32
   unsigned int* tail_counters;  // [tail tile][CTA of the pair], zero between launches
+  // Fused epilogue (instances with Cfg::kEpi only), per element in fp32:
+  //   D = act(alpha * acc + bias[col]) + beta * residual[row][col]
+  // then rounded to bf16 (RNE) or stored as fp32 (out_f32).
+  uint32_t epi_flags;          // kEpiBias | kEpiResidual
+  int act;                     // kAct*
+  int out_f32;                 // 1: C holds fp32, ldc in fp32 elements
+  float alpha, beta;
+  const uint16_t* bias;        // bf16[N]
+  const uint16_t* residual;    // bf16, row pitch ldr elements
+  long long ldr;
 };
+
+constexpr uint32_t kEpiBias = 1u;
+constexpr uint32_t kEpiResidual = 2u;
+constexpr int kActNone = 0, kActRelu = 1, kActGelu = 2, kActGeluTanh = 3, kActSilu = 4;
 
 // One work unit of a CTA pair: a tile and a K range; slot >= 0 marks a K
 // slice of a split tile (its index among the tail units).
@@ -126,12 +140,15 @@ __device__ __forceinline__ WorkUnit unit_at(const GemmParams& p, uint32_t u) {
 //   MN (NB = 1 only): columns of one MMA and of the tile, a multiple of 32
 //           up to 256 (e.g. 224 = 1792 / 8 for an N-sharded MLP projection),
 //           so the tile width can divide N and fill the last wave.
-template <int STAGES, int NB, int MN = 256>
+//   EPI:    fused epilogue (bias, activation, residual, fp32 output) compiled
+//           in; the plain instances carry none of its code.
+template <int STAGES, int NB, int MN = 256, bool EPI = false>
 struct GemmCfg {
   static_assert(NB == 1 || NB == 2, "one or two MMA column blocks per tile");
   static_assert(MN % 32 == 0 && MN >= 64 && MN <= 256 && (NB == 1 || MN == 256), "MMA width");
   static constexpr int kStages = STAGES;
   static constexpr int kNB = NB;
+  static constexpr bool kEpi = EPI;
   static constexpr int kMmaN = MN;                       // columns per tcgen05.mma
   static constexpr int kBRows = MN / 2;                  // B rows per CTA per column block
   static constexpr int kBlockBytesB = kBRows * kBlockK * 2;
@@ -174,28 +191,39 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
   return kSmemDescHi | uint64_t((addr & 0x3FFFFu) >> 4);
 }
 
-// Write one 32-row x 32-column chunk of C held as packed bf16 pairs (lane =
-// row, pk[i] = columns 2i, 2i+1).  Full chunks go through a 64-byte-swizzled
-// staging buffer (16-byte group j of row r sits at group j ^ ((r >> 1) & 3),
-// so the eight rows of each shared-memory wavefront hit distinct banks) and a
-// TMA store.  TMA clips the innermost dimension in 16-byte units, so the
-// chunk that ends inside a 16-byte group (N % 8 != 0) is written with plain
-// per-element predicated stores instead.
-template <class Cfg>
-__device__ __forceinline__ void store_c_chunk(const uint32_t (&pk)[16], int col, int row,
+// Write one 32-row x 64-byte chunk of C: lane = row, w[] = the row's 16
+// 32-bit words, i.e. 32 bf16 columns (packed pairs, ESIZE 2) or 16 fp32
+// columns (ESIZE 4) starting at `col`.  Full chunks go through a 64-byte-
+// swizzled staging buffer (16-byte group j of row r sits at group
+// j ^ ((r >> 1) & 3), so the eight rows of each shared-memory wavefront hit
+// distinct banks) and a TMA store.  TMA clips the innermost dimension in
+// 16-byte units, so the chunk that ends inside a 16-byte group (N not a
+// multiple of 16 / ESIZE) is written with per-element predicated stores.
+template <class Cfg, int ESIZE = 2>
+__device__ __forceinline__ void store_c_chunk(const uint32_t (&w)[16], int col, int row,
                                               uint32_t lane, uint32_t cstage0, uint32_t& cbuf,
                                               const CUtensorMap& map_c, const GemmParams& p) {
+  static_assert(ESIZE == 2 || ESIZE == 4, "bf16 or fp32 C");
+  constexpr int kCols = 64 / ESIZE;        // columns per chunk
+  constexpr int kGroup = 16 / ESIZE;       // columns per 16-byte group
   const bool store = (row < p.M) && (col < p.N);  // warp-uniform
-  const bool ragged = ((p.N & 7) != 0) && (col + kCBoxCols > p.N);
+  const bool ragged = ((p.N % kGroup) != 0) && (col + kCols > p.N);
   if (store && ragged) {
     const int r = row + static_cast<int>(lane);
     if (r < p.M) {
-      uint16_t* dst = p.C + static_cast<long long>(r) * p.ldc + col;
       const int ncols = p.N - col;
+      if constexpr (ESIZE == 2) {
+        uint16_t* dst = p.C + static_cast<long long>(r) * p.ldc + col;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        if (2 * i < ncols) dst[2 * i] = static_cast<uint16_t>(pk[i] & 0xFFFFu);
-        if (2 * i + 1 < ncols) dst[2 * i + 1] = static_cast<uint16_t>(pk[i] >> 16);
+        for (int i = 0; i < 16; ++i) {
+          if (2 * i < ncols) dst[2 * i] = static_cast<uint16_t>(w[i] & 0xFFFFu);
+          if (2 * i + 1 < ncols) dst[2 * i + 1] = static_cast<uint16_t>(w[i] >> 16);
+        }
+      } else {
+        uint32_t* dst = reinterpret_cast<uint32_t*>(p.C) + static_cast<long long>(r) * p.ldc + col;
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          if (i < ncols) dst[i] = w[i];
       }
     }
   } else if (store) {
@@ -207,8 +235,8 @@ __device__ __forceinline__ void store_c_chunk(const uint32_t (&pk)[16], int col,
     const uint32_t sw = (lane >> 1) & 3u;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      ptx::st_shared_v4(rowaddr + ((static_cast<uint32_t>(j) ^ sw) << 4), pk[4 * j], pk[4 * j + 1],
-                        pk[4 * j + 2], pk[4 * j + 3]);
+      ptx::st_shared_v4(rowaddr + ((static_cast<uint32_t>(j) ^ sw) << 4), w[4 * j], w[4 * j + 1],
+                        w[4 * j + 2], w[4 * j + 3]);
     }
     ptx::fence_proxy_async_smem();
     __syncwarp();
@@ -225,15 +253,152 @@ __device__ __forceinline__ void store_c_chunk(const uint32_t (&pk)[16], int col,
         const uint32_t r = seg >> 2, q = seg & 3u;
         uint32_t x0, x1, x2, x3;
         ptx::ld_shared_v4(buf + r * 64u + ((q ^ ((r >> 1) & 3u)) << 4), x0, x1, x2, x3);
-        const int grow = row + static_cast<int>(r), gcol = col + static_cast<int>(q) * 8;
+        const int grow = row + static_cast<int>(r), gcol = col + static_cast<int>(q) * kGroup;
         if (grow < p.M && gcol < p.N) {
-          const long long off = (static_cast<long long>(grow) * p.ldc + gcol) * 2;
+          const long long off = (static_cast<long long>(grow) * p.ldc + gcol) * ESIZE;
           for (int i = 0; i < p.npeers; ++i) ptx::st_global_v4(p.peer_c[i] + off, x0, x1, x2, x3);
         }
       }
     }
     if (++cbuf == Cfg::kCBufs) cbuf = 0;
   }
+}
+
+// bf16 bits -> fp32.
+__device__ __forceinline__ float bf16_lo(uint32_t x) { return __uint_as_float(x << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t x) { return __uint_as_float(x & 0xFFFF0000u); }
+
+// Eight bf16 values src[col .. col + 7] as four packed pairs; columns at or
+// past N read as 0.  The vector path needs src 16-byte aligned at col
+// (checked on the host for bias and residual rows; col is a multiple of 8).
+__device__ __forceinline__ void load_bf16x8(const uint16_t* src, int col, int N, uint32_t (&w)[4]) {
+  if (col + 8 <= N) {
+    ptx::ld_global_nc_v4(src + col, w[0], w[1], w[2], w[3]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t lo = (col + 2 * i < N) ? __ldg(src + col + 2 * i) : 0u;
+      const uint32_t hi = (col + 2 * i + 1 < N) ? __ldg(src + col + 2 * i + 1) : 0u;
+      w[i] = lo | (hi << 16);
+    }
+  }
+}
+
+// Epilogue operands of one epilogue warp for one tile, loaded before the
+// warp waits for the tile's accumulator so their latency hides behind it:
+// the bias of the warp's MMA column block (lane l holds columns 8l .. 8l+7,
+// handed to the other lanes by shuffles) and the residual row of the first
+// 32-column chunk (then each next chunk's while the current one is done).
+__device__ __forceinline__ void epi_load_bias(const GemmParams& p, int col0, int ncols, uint32_t lane,
+                                              uint32_t (&bias_w)[4]) {
+  const int c = col0 + 8 * static_cast<int>(lane);
+  if ((p.epi_flags & kEpiBias) && 8 * static_cast<int>(lane) < ncols && c < p.N) {
+    load_bf16x8(p.bias, c, p.N, bias_w);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) bias_w[i] = 0u;
+  }
+}
+
+__device__ __forceinline__ void epi_load_residual(const GemmParams& p, int r, int col, uint32_t (&q)[16]) {
+  if ((p.epi_flags & kEpiResidual) && r < p.M && col < p.N) {
+    const uint16_t* src = p.residual + static_cast<long long>(r) * p.ldr;
+    if (col + 32 <= p.N && (reinterpret_cast<uintptr_t>(src + col) & 31u) == 0) {
+      // two 32-byte loads: half the L1 wavefronts of four 16-byte ones
+      uint32_t w0[8], w1[8];
+      ptx::ld_global_nc_v8(src + col, w0);
+      ptx::ld_global_nc_v8(src + col + 16, w1);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        q[i] = w0[i];
+        q[8 + i] = w1[i];
+      }
+      return;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint32_t w[4];
+      load_bf16x8(src, col + 8 * j, p.N, w);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) q[4 * j + i] = w[i];
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) q[i] = 0u;
+  }
+}
+
+// The fused epilogue on one lane's 32 accumulators (chunk `c` of the warp's
+// column block), in place, fp32 throughout:
+//   D = act(alpha * acc + bias[col]) + beta * residual[r][col].
+// GELU is 0.5 x (1 + erf(x / sqrt 2)) or its tanh form
+// 0.5 x (1 + tanh(sqrt(2 / pi) (x + 0.044715 x^3))) (Hendrycks & Gimpel);
+// SiLU is x / (1 + e^-x).  For fp32 output the transcendentals are CUDA's
+// erff / tanhf / expf; for bf16 output, whose spacing (2^-8 relative) is far
+// coarser than their error, tanh and the reciprocal are the hardware
+// approximations (tanh.approx, rcp.approx) and e^x is __expf.  erf is erff
+// for both.
+__device__ __forceinline__ void apply_epilogue(uint32_t (&v)[32], int c, const uint32_t (&bias_w)[4],
+                                               const uint32_t (&res_w)[16], const GemmParams& p) {
+  float d[32];
+#pragma unroll
+  for (int k = 0; k < 32; ++k) d[k] = p.alpha * __uint_as_float(v[k]);
+  if (p.epi_flags & kEpiBias) {
+#pragma unroll
+    for (int q = 0; q < 16; ++q) {
+      // columns 32c + 2q, +1 live in lane 4c + q / 4, word q % 4
+      const uint32_t b = __shfl_sync(0xFFFFFFFFu, bias_w[q & 3], 4 * c + (q >> 2));
+      d[2 * q] += bf16_lo(b);
+      d[2 * q + 1] += bf16_hi(b);
+    }
+  }
+  const bool fast = p.out_f32 == 0;
+  switch (p.act) {
+    case kActRelu:
+#pragma unroll
+      for (int k = 0; k < 32; ++k) d[k] = fmaxf(d[k], 0.0f);
+      break;
+    case kActGelu:
+#pragma unroll
+      for (int k = 0; k < 32; ++k) d[k] = 0.5f * d[k] * (1.0f + erff(d[k] * 0.70710678118654752f));
+      break;
+    case kActGeluTanh:
+      if (fast) {
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+          const float x = d[k];
+          const float u = 0.79788456080286536f * fmaf(0.044715f * x, x * x, x);
+          d[k] = 0.5f * x * (1.0f + ptx::tanh_approx(u));
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+          const float x = d[k];
+          d[k] = 0.5f * x * (1.0f + tanhf(0.79788456080286536f * (x + 0.044715f * x * x * x)));
+        }
+      }
+      break;
+    case kActSilu:
+      if (fast) {
+#pragma unroll
+        for (int k = 0; k < 32; ++k) d[k] = d[k] * ptx::rcp_approx(1.0f + __expf(-d[k]));
+      } else {
+#pragma unroll
+        for (int k = 0; k < 32; ++k) d[k] = d[k] / (1.0f + expf(-d[k]));
+      }
+      break;
+    default:
+      break;
+  }
+  if (p.epi_flags & kEpiResidual) {
+#pragma unroll
+    for (int q = 0; q < 16; ++q) {
+      d[2 * q] = fmaf(p.beta, bf16_lo(res_w[q]), d[2 * q]);
+      d[2 * q + 1] = fmaf(p.beta, bf16_hi(res_w[q]), d[2 * q + 1]);
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 32; ++k) v[k] = __float_as_uint(d[k]);
 }
 
 template <class Cfg>
@@ -397,15 +562,30 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
       const WorkUnit cur = nxt;
       if (t + nclusters < num_units) nxt = unit_at(p, t + nclusters);
       const uint32_t tile = cur.tile;
+      const int row = static_cast<int>(tile >> 16) * kTileM + static_cast<int>(rank) * 128 +
+                      static_cast<int>(quarter) * 32;
+      const int col0 = static_cast<int>(tile & 0xFFFFu) * Cfg::kTileN + static_cast<int>(nblk) * Cfg::kMmaN;
+      [[maybe_unused]] uint32_t bias_w[4];
+      [[maybe_unused]] uint32_t res_w[16];
+      if constexpr (Cfg::kEpi) {
+        const int r = row + static_cast<int>(lane);
+        if ((p.epi_flags & kEpiResidual) && r < p.M) {
+          // This lane's residual row for the whole column block, into L2 while
+          // the MMAs run, so the per-chunk loads below wait on L2, not DRAM.
+          const uint16_t* src = p.residual + static_cast<long long>(r) * p.ldr;
+#pragma unroll
+          for (int b = 1; b < (Cfg::kMmaN * 2 + 127) / 128; ++b)
+            if (col0 + 64 * b < p.N) ptx::prefetch_l2(src + col0 + 64 * b);
+        }
+        epi_load_bias(p, col0, Cfg::kMmaN, lane, bias_w);
+        epi_load_residual(p, r, col0, res_w);
+      }
       // After a timeout (here or in another role) the loop keeps running
       // without doing work, so every epilogue warp still reaches every named
       // barrier of the K-slice path below; later waits fail immediately.
       const bool full_ok = ptx::mbar_wait(tfull0 + 8 * acc, acc_phase, wd, kSiteEpilogue, t);
       const bool live = __all_sync(0xFFFFFFFFu, full_ok);  // warp-uniform
       ptx::tc_fence_after();
-      const int row = static_cast<int>(tile >> 16) * kTileM + static_cast<int>(rank) * 128 +
-                      static_cast<int>(quarter) * 32;
-      const int col0 = static_cast<int>(tile & 0xFFFFu) * Cfg::kTileN + static_cast<int>(nblk) * Cfg::kMmaN;
       const uint32_t t_row =
           tmem_base + ((quarter * 32u) << 16) + acc * Cfg::kAccStride + nblk * Cfg::kMmaN;
       if (cur.slot < 0 && !live) {
@@ -413,9 +593,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
       } else if (cur.slot < 0) {
         // Whole tile: chunks of 32 columns: TMEM -> registers -> bf16 ->
         // swizzled staging buffer -> TMA store, two buffers in flight per warp.
-#pragma unroll 1
-        for (int c = 0; c < Cfg::kChunks; ++c) {
-          uint32_t v[32];
+        auto tmem_chunk = [&](int c, uint32_t (&v)[32]) {
           ptx::tmem_ld_32x32b_x32(t_row + c * kCBoxCols, v);
           ptx::tmem_wait_ld();
           ptx::reg_fence32(v);
@@ -425,12 +603,51 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
             __syncwarp();
             if (lane == 0) ptx::mbar_arrive_cluster(tempty_leader0 + 8 * acc);
           }
+        };
+        auto store_bf16 = [&](int c, const uint32_t (&v)[32]) {
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) pk[i] = ptx::pack_bf16x2(v[2 * i], v[2 * i + 1]);
           store_c_chunk<Cfg>(pk, col0 + c * kCBoxCols, row, lane, cstage0, cbuf, map_c, p);
+        };
+        if constexpr (Cfg::kEpi) {
+          // The residual of chunk c + 1 loads while chunk c is finished; two
+          // buffers take turns so no register copy waits on those loads.
+          uint32_t res_b[16];
+          auto chunk = [&](int c, const uint32_t (&cur)[16], uint32_t (&nxt)[16]) {
+            if (c + 1 < Cfg::kChunks)
+              epi_load_residual(p, row + static_cast<int>(lane), col0 + (c + 1) * kCBoxCols, nxt);
+            uint32_t v[32];
+            tmem_chunk(c, v);
+            apply_epilogue(v, c, bias_w, cur, p);
+            if (p.out_f32) {
+              uint32_t lo[16], hi[16];
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                lo[i] = v[i];
+                hi[i] = v[16 + i];
+              }
+              const int col = col0 + c * kCBoxCols;
+              store_c_chunk<Cfg, 4>(lo, col, row, lane, cstage0, cbuf, map_c, p);
+              store_c_chunk<Cfg, 4>(hi, col + 16, row, lane, cstage0, cbuf, map_c, p);
+            } else {
+              store_bf16(c, v);
+            }
+          };
+#pragma unroll 1
+          for (int c = 0; c < Cfg::kChunks; c += 2) {
+            chunk(c, res_w, res_b);
+            if (c + 1 < Cfg::kChunks) chunk(c + 1, res_b, res_w);
+          }
+        } else {
+#pragma unroll 1
+          for (int c = 0; c < Cfg::kChunks; ++c) {
+            uint32_t v[32];
+            tmem_chunk(c, v);
+            store_bf16(c, v);
+          }
         }
-      } else {
+      } else if constexpr (!Cfg::kEpi) {
         // K slice of a split tile.  Partials are laid out so that the 32
         // threads of a warp (32 consecutive rows) touch 512 contiguous bytes
         // per 16-byte column group: [column group][row 0..127] of float4.

@@ -386,6 +386,41 @@ __device__ __forceinline__ void ld_global_cg_v4(const void* ptr, uint32_t& a, ui
                : "memory");
 }
 
+// Hint: bring the 128-byte line holding `ptr` into L2.
+__device__ __forceinline__ void prefetch_l2(const void* ptr) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
+}
+
+// Hardware approximations (one MUFU operation each): tanh with relative
+// error about 2^-11 and the reciprocal, both ISA instructions.
+__device__ __forceinline__ float tanh_approx(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// 16-byte load of data that stays unchanged for the whole kernel (bias,
+// residual) through the non-coherent path.
+__device__ __forceinline__ void ld_global_nc_v4(const void* ptr, uint32_t& a, uint32_t& b, uint32_t& c,
+                                                uint32_t& d) {
+  asm volatile("ld.global.nc.L1::no_allocate.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(a), "=r"(b), "=r"(c), "=r"(d)
+               : "l"(ptr));
+}
+
+// 32-byte load (256-bit access; `ptr` 32-byte aligned), non-coherent path.
+__device__ __forceinline__ void ld_global_nc_v8(const void* ptr, uint32_t (&w)[8]) {
+  asm volatile("ld.global.nc.L1::no_allocate.v8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]), "=r"(w[4]), "=r"(w[5]), "=r"(w[6]),
+                 "=r"(w[7])
+               : "l"(ptr));
+}
+
 // Barrier over `count` threads (a multiple of 32) of this CTA on named barrier `id`.
 __device__ __forceinline__ void named_barrier(uint32_t id, uint32_t count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");

@@ -67,6 +67,9 @@ def parse_args(argv=None):
                    help="also time an NCCL all-gather of the C shards (separately)")
     p.add_argument("--fused-allgather", action="store_true",
                    help="also time the GEMM with the all-gather fused into its epilogue")
+    p.add_argument("--epilogue", default=None, choices=["relu", "gelu", "gelu_tanh", "silu"],
+                   help="also time GEMM + bias + this activation fused into the epilogue, against "
+                        "cuBLASLt's fused bias+GELU/ReLU epilogue and the unfused torch sequence")
     p.add_argument("--no-cublas", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
@@ -193,6 +196,50 @@ def time_steps(torch, step, steps, flush, stream, dev, barrier):
     ms = sum(e0.elapsed_time(e1) for e0, e1 in pairs)
     del scratch
     return ms
+
+
+def time_epilogue(gemm, torch, A, B, C, args, flush, stream, dev, barrier, flops):
+    """GEMM + bias + activation: ours fused (b200gemm_bf16_nt_epilogue), cuBLASLt's
+    fused epilogue (torch._addmm_activation: bias + GELU(tanh) or ReLU), and the
+    unfused torch sequence (matmul, then bias + activation kernels)."""
+    import torch.nn.functional as F
+
+    act = args.epilogue
+    N = B.shape[0]
+    g = torch.Generator(device=dev)
+    g.manual_seed(args.seed + 7)
+    bias = (torch.randn(N, generator=g, device=dev) * 0.1).to(torch.bfloat16)
+    out = torch.empty_like(C)
+    steps = max(3, min(args.steps, 20))
+    res = {"activation": act, "bias": True, "steps": steps}
+
+    def tflops(ms):
+        return flops / (ms / 1e3 / steps) / 1e12
+
+    ours = lambda: gemm.bf16_nt_epilogue(A, B, bias=bias, activation=act, out=out)  # noqa: E731
+    for _ in range(3):
+        ours()
+    barrier()
+    res["ours_tflops"] = tflops(time_steps(torch, ours, steps, flush, stream, dev, barrier))
+    torch.backends.cuda.preferred_blas_library("cublaslt")
+    Bt = B.t()
+    if act in ("relu", "gelu_tanh"):
+        lt = lambda: torch._addmm_activation(bias, A, Bt, use_gelu=(act != "relu"))  # noqa: E731
+        for _ in range(3):
+            lt()
+        barrier()
+        res["cublaslt_fused_tflops"] = tflops(time_steps(torch, lt, steps, flush, stream, dev, barrier))
+    fn = {"relu": F.relu, "gelu": F.gelu, "silu": F.silu,
+          "gelu_tanh": lambda x: F.gelu(x, approximate="tanh")}[act]
+    unfused = lambda: fn(torch.matmul(A, Bt) + bias)  # noqa: E731
+    for _ in range(3):
+        unfused()
+    barrier()
+    res["unfused_torch_tflops"] = tflops(time_steps(torch, unfused, steps, flush, stream, dev, barrier))
+    res["how"] = ("TFLOPS of the GEMM flops (2MNK) per step, steps timed like `value`; cuBLASLt fused = "
+                  "torch._addmm_activation (cuBLASLt bias+GELU(tanh)/ReLU epilogue), unfused = "
+                  "torch.matmul then bias add and activation as separate kernels")
+    return res
 
 
 def roofline(w, M, N, K, ms_per_launch, peaks, peak_kind, traffic):
@@ -390,6 +437,11 @@ def run_ours(args, w):
                              "per_gpu": True, "how": "torch.matmul, preferred_blas_library=cublaslt; "
                                                      "timed exactly like `value` (same L2 rule)"}
         del Cr
+
+    # ------------------------------- GEMM + bias + activation in the epilogue
+    if args.epilogue and not library_arm:
+        extra["epilogue"] = time_epilogue(gemm, torch, A, B, C, args, flush, stream, dev, barrier,
+                                          flops_rank)
 
     # ---------------------------------------- optional all-gather of C shards
     if args.allgather and distributed:

@@ -53,6 +53,44 @@ void b200gemm_destroy(b200gemm_t handle);
 int b200gemm_bf16_nt(b200gemm_t handle, int M, int N, int K, const void* A, const void* B,
                      void* C, int ldc, void* stream);
 
+/* Fused epilogue, applied per element in fp32 to the accumulator before C is
+ * written (the ops around an MLP projection, without a second pass over C):
+ *     D[i][j] = act(alpha * (A . B^T)[i][j] + bias[j]) + beta * residual[i][j]
+ * then C[i][j] = D[i][j] rounded to bf16 (RNE) or stored as fp32.  A NULL
+ * bias or residual drops that term.  No counterpart in the reference, whose
+ * epilogue only rounds the accumulator to bf16 (matmul_1.cuh:293-295). */
+#define B200GEMM_ACT_NONE 0
+#define B200GEMM_ACT_RELU 1       /* max(x, 0)                                   */
+#define B200GEMM_ACT_GELU 2       /* 0.5 x (1 + erf(x / sqrt 2))                 */
+#define B200GEMM_ACT_GELU_TANH 3  /* 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))) */
+#define B200GEMM_ACT_SILU 4       /* x / (1 + exp(-x))                           */
+#define B200GEMM_OUT_BF16 0
+#define B200GEMM_OUT_F32 1
+typedef struct b200gemm_epilogue {
+  float alpha;           /* scale of A . B^T                                     */
+  float beta;            /* scale of the residual                                */
+  const void* bias;      /* bf16[N] device vector, 16-byte aligned, or NULL      */
+  const void* residual;  /* bf16 M x N device matrix, row pitch ldr, or NULL     */
+  int ldr;               /* residual pitch in elements: ldr >= N, ldr % 8 == 0,  */
+                         /* residual 16-byte aligned                             */
+  int activation;        /* B200GEMM_ACT_*                                       */
+  int out_type;          /* B200GEMM_OUT_BF16 or B200GEMM_OUT_F32 (C holds fp32, */
+                         /* ldc in fp32 elements, ldc % 4 == 0)                  */
+  int reserved;          /* set to 0                                             */
+} b200gemm_epilogue;
+
+/* C = epilogue(A . B^T) with the epilogue above; epi == NULL is exactly
+ * b200gemm_bf16_nt.  Same rules as b200gemm_bf16_nt, plus K > 0 and those in
+ * the struct.  Always runs the tiled kernel (at any M); its tile width
+ * accounts for the epilogue's cost (a costly epilogue favours 256-wide
+ * tiles, whose epilogue overlaps the next tile's MMAs).  Every tile width
+ * sums an element's K products in the same order, so the accumulator is
+ * bit-identical to b200gemm_bf16_nt's whenever that call runs the tiled
+ * kernel (M > 128, or the small-M kernel switched off). */
+int b200gemm_bf16_nt_epilogue(b200gemm_t handle, int M, int N, int K, const void* A,
+                              const void* B, void* C, int ldc, const b200gemm_epilogue* epi,
+                              void* stream);
+
 /* C = A . B^T with A, B and C in host memory (pinned memory lets the copies
  * overlap; pageable memory works but serialises).  The handle stages the
  * operands in device buffers it owns (allocated on first use, grown when

@@ -219,3 +219,49 @@ int oracle_gemm_bf16_nt_f32(int M, int N, int K, const uint16_t* A, const uint16
 }
 
 int oracle_num_cpus(void) { return default_threads(0); }
+
+/* ------------------------------------------------- fused epilogue (fp64)
+ * Restatement of the library's optional fused epilogue, which has no
+ * counterpart in the reference (whose epilogue is only the bf16 rounding of
+ * matmul_1.cuh:293-295).  On an fp64 GEMM sum s of element (i, j):
+ *   d = act(alpha * s + bias[j]) + beta * R[i][j]
+ * with act: 0 none, 1 max(x, 0), 2 0.5 x (1 + erf(x / sqrt 2)),
+ * 3 0.5 x (1 + tanh(sqrt(2 / pi) (x + 0.044715 x^3))), 4 x / (1 + exp(-x)),
+ * evaluated in fp64 with the C library's erf, tanh and exp.  bias (bf16[N])
+ * and R (bf16, row pitch ldr) may be NULL. */
+static double epi_act(double x, int act) {
+  switch (act) {
+    case 1: return x > 0.0 ? x : 0.0;
+    case 2: return 0.5 * x * (1.0 + erf(x * 0.70710678118654752440));
+    case 3: return 0.5 * x * (1.0 + tanh(0.79788456080286535588 * (x + 0.044715 * x * x * x)));
+    case 4: return x / (1.0 + exp(-x));
+    default: return x;
+  }
+}
+
+static inline double epi_one(double s, int i, int j, double alpha, const uint16_t* bias, int act,
+                             const uint16_t* R, int ldr, double beta) {
+  double d = alpha * s;
+  if (bias) d += (double)bf16_to_f32(bias[j]);
+  d = epi_act(d, act);
+  if (R) d += beta * (double)bf16_to_f32(R[(size_t)i * ldr + j]);
+  return d;
+}
+
+/* In place on D (M x N, row pitch ldd) holding fp64 GEMM sums. */
+void oracle_epilogue_f64(double* D, int M, int N, int ldd, double alpha, const uint16_t* bias,
+                         int act, const uint16_t* R, int ldr, double beta) {
+  for (int i = 0; i < M; ++i)
+    for (int j = 0; j < N; ++j) {
+      double* x = D + (size_t)i * ldd + j;
+      *x = epi_one(*x, i, j, alpha, bias, act, R, ldr, beta);
+    }
+}
+
+/* In place on sampled sums vals[s] of elements (rows[s], cols[s]). */
+void oracle_epilogue_sampled(double* vals, const int* rows, const int* cols, size_t count,
+                             double alpha, const uint16_t* bias, int act, const uint16_t* R,
+                             int ldr, double beta) {
+  for (size_t s = 0; s < count; ++s)
+    vals[s] = epi_one(vals[s], rows[s], cols[s], alpha, bias, act, R, ldr, beta);
+}

@@ -62,6 +62,11 @@ def lib():
                                                   c_int, c_int, c_int]
             L.oracle_gemm_bf16_nt_f32.restype = c_int
             L.oracle_num_cpus.restype = c_int
+            vp, c_double = ctypes.c_void_p, ctypes.c_double
+            L.oracle_epilogue_f64.argtypes = [_f64p, c_int, c_int, c_int, c_double, vp, c_int, vp,
+                                              c_int, c_double]
+            L.oracle_epilogue_sampled.argtypes = [_f64p, _i32p, _i32p, c_size, c_double, vp, c_int,
+                                                  vp, c_int, c_double]
             _lib = L
         return _lib
 
@@ -131,6 +136,47 @@ def gemm_f32_cpu(A, B, row_begin: int = 0, row_end: int | None = None, threads: 
     if used < 0:
         raise ValueError("oracle_gemm_bf16_nt_f32: bad arguments or out of memory")
     return C[row_begin:row_end], used
+
+
+ACTIVATIONS = {"none": 0, "relu": 1, "gelu": 2, "gelu_tanh": 3, "silu": 4}
+
+
+def _opt_bits(x):
+    """(keep-alive array, pointer) for an optional bf16 bit array."""
+    if x is None:
+        return None, None
+    arr = np.ascontiguousarray(x, dtype=np.uint16)
+    return arr, arr.ctypes.data
+
+
+def epilogue_f64(S, alpha=1.0, bias=None, act="none", residual=None, beta=1.0) -> np.ndarray:
+    """D = act(alpha S + bias[j]) + beta R[i][j] on fp64 sums S [M, N] (a copy;
+    bias: bf16 bits [N], residual: bf16 bits [M, N] or None)."""
+    D = np.array(S, dtype=np.float64, order="C", copy=True)
+    M, N = D.shape
+    b, bp = _opt_bits(bias)
+    r, rp = _opt_bits(residual)
+    if b is not None:
+        assert b.shape == (N,)
+    if r is not None:
+        assert r.shape == (M, N)
+    lib().oracle_epilogue_f64(D, M, N, max(N, 1), float(alpha), bp, ACTIVATIONS[act], rp, max(N, 1),
+                              float(beta))
+    return D
+
+
+def epilogue_sampled(vals, rows, cols, alpha=1.0, bias=None, act="none", residual=None,
+                     beta=1.0) -> np.ndarray:
+    """The same on sampled sums vals[s] of elements (rows[s], cols[s])."""
+    out = np.array(vals, dtype=np.float64, copy=True)
+    rows = np.ascontiguousarray(rows, dtype=np.int32)
+    cols = np.ascontiguousarray(cols, dtype=np.int32)
+    b, bp = _opt_bits(bias)
+    r, rp = _opt_bits(residual)
+    ldr = r.shape[1] if r is not None else 1
+    lib().oracle_epilogue_sampled(out, rows, cols, out.shape[0], float(alpha), bp, ACTIVATIONS[act],
+                                  rp, ldr, float(beta))
+    return out
 
 
 def num_cpus() -> int:

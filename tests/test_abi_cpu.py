@@ -44,6 +44,10 @@ def test_null_handle_is_rejected_without_cuda():
     assert lib.b200gemm_last_device_status(None, None) == _lib.ERR_INVALID_ARG
     assert lib.b200gemm_selftest_watchdog(None, 1, None) == _lib.ERR_INVALID_ARG
     assert lib.b200gemm_create(None, 0) == _lib.ERR_INVALID_ARG
+    epi = _lib.Epilogue(alpha=1.0)
+    assert lib.b200gemm_bf16_nt_epilogue(None, 1, 1, 8, None, None, None, 8, ctypes.byref(epi),
+                                         None) == _lib.ERR_INVALID_ARG
+    assert ctypes.sizeof(_lib.Epilogue) == 40  # the header's struct layout on LP64
     lib.b200gemm_destroy(None)
 
 

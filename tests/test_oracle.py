@@ -113,3 +113,36 @@ def test_generators_are_seeded(dist):
         assert np.abs(bf).max() < 0.2
     if dist == "uniform":
         assert np.abs(bf).max() <= 1.0
+
+
+@pytest.mark.parametrize("act", ["none", "relu", "gelu", "gelu_tanh", "silu"])
+def test_epilogue_restatement(oracle_mod, act):
+    """The C restatement of the fused epilogue against an independent numpy /
+    scipy evaluation of the same formulas, full and sampled."""
+    from scipy.special import erf
+
+    o = oracle_mod
+    rng = np.random.Generator(np.random.PCG64(4))
+    M, N = 37, 53
+    S = rng.standard_normal((M, N)) * 6.0
+    bias = data.f32_to_bf16_bits(rng.standard_normal(N).astype(np.float32))
+    res = data.f32_to_bf16_bits(rng.standard_normal((M, N)).astype(np.float32))
+    alpha, beta = 0.75, -1.5
+    x = alpha * S + data.bf16_bits_to_f32(bias).astype(np.float64)[None, :]
+    f = {
+        "none": lambda v: v,
+        "relu": lambda v: np.maximum(v, 0.0),
+        "gelu": lambda v: 0.5 * v * (1.0 + erf(v / np.sqrt(2.0))),
+        "gelu_tanh": lambda v: 0.5 * v * (1.0 + np.tanh(np.sqrt(2.0 / np.pi) * (v + 0.044715 * v ** 3))),
+        "silu": lambda v: v / (1.0 + np.exp(-v)),
+    }[act]
+    want = f(x) + beta * data.bf16_bits_to_f32(res).astype(np.float64)
+    got = o.epilogue_f64(S, alpha=alpha, bias=bias, act=act, residual=res, beta=beta)
+    assert np.allclose(got, want, rtol=1e-12, atol=1e-12)
+    rows = rng.integers(0, M, 200).astype(np.int32)
+    cols = rng.integers(0, N, 200).astype(np.int32)
+    got_s = o.epilogue_sampled(S[rows, cols], rows, cols, alpha=alpha, bias=bias, act=act,
+                               residual=res, beta=beta)
+    assert np.allclose(got_s, want[rows, cols], rtol=1e-12, atol=1e-12)
+    # no bias, no residual: only the scale and the activation
+    assert np.allclose(o.epilogue_f64(S, alpha=alpha, act=act), f(alpha * S), rtol=1e-12, atol=1e-12)
