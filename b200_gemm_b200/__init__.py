@@ -107,13 +107,14 @@ class Gemm:
 
     def bf16_nt_epilogue(self, A, B, bias=None, activation: str = "none", residual=None,
                          alpha: float = 1.0, beta: float = 1.0, out=None, out_dtype=None,
-                         stream=None):
+                         out_scale: float = 1.0, stream=None):
         """out = act(alpha * A @ B^T + bias) + beta * residual, fused into the
         GEMM's epilogue (fp32 math, one pass over C).
 
         bias: bf16 [N] CUDA tensor or None; residual: bf16 [M, N] row-major
         view (row stride = ldr) or None; activation: none, relu, gelu,
-        gelu_tanh, silu; out_dtype: torch.bfloat16 (default) or torch.float32.
+        gelu_tanh, silu; out_dtype: torch.bfloat16 (default), torch.float32,
+        or torch.float8_e4m3fn (stores e4m3(out_scale * D), saturating).
         """
         import torch
 
@@ -129,9 +130,11 @@ class Gemm:
         N = B.shape[0]
         if out_dtype is None:
             out_dtype = out.dtype if out is not None else torch.bfloat16
-        if out_dtype not in (torch.bfloat16, torch.float32):
-            raise TypeError("out_dtype must be torch.bfloat16 or torch.float32")
-        group = 8 if out_dtype == torch.bfloat16 else 4  # elements per 16 bytes
+        kinds = {torch.bfloat16: (_lib.OUT_BF16, 8), torch.float32: (_lib.OUT_F32, 4),
+                 torch.float8_e4m3fn: (_lib.OUT_E4M3, 16)}
+        if out_dtype not in kinds:
+            raise TypeError("out_dtype must be torch.bfloat16, torch.float32 or torch.float8_e4m3fn")
+        out_type, group = kinds[out_dtype]  # group: elements per 16 bytes
         if out is None:
             pitch = group * ((N + group - 1) // group)
             out = torch.empty(M, pitch, device=A.device, dtype=out_dtype)[:, :N]
@@ -139,7 +142,7 @@ class Gemm:
             raise ValueError("out must be an [M, N] row-major view of out_dtype")
         ldc = out.stride(0) if M > 1 else group * ((N + group - 1) // group)
         epi = _lib.Epilogue(alpha=float(alpha), beta=float(beta), activation=_ACTIVATIONS[activation],
-                            out_type=_lib.OUT_F32 if out_dtype == torch.float32 else _lib.OUT_BF16)
+                            out_type=out_type, out_scale=float(out_scale))
         if bias is not None:
             if bias.dtype != torch.bfloat16 or tuple(bias.shape) != (N,) or bias.stride(0) != 1:
                 raise ValueError("bias must be a contiguous bf16 [N] tensor")

@@ -24,7 +24,7 @@ ORDER_HILBERT = 0
 ORDER_BANDS = 1
 
 ACT_NONE, ACT_RELU, ACT_GELU, ACT_GELU_TANH, ACT_SILU = 0, 1, 2, 3, 4
-OUT_BF16, OUT_F32 = 0, 1
+OUT_BF16, OUT_F32, OUT_E4M3 = 0, 1, 2
 
 _c_int, _c_uint, _c_ull, _vp = ctypes.c_int, ctypes.c_uint, ctypes.c_ulonglong, ctypes.c_void_p
 
@@ -39,7 +39,7 @@ class Epilogue(ctypes.Structure):
         ("ldr", _c_int),
         ("activation", _c_int),
         ("out_type", _c_int),
-        ("reserved", _c_int),
+        ("out_scale", ctypes.c_float),
     ]
 
 

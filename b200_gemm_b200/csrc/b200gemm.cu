@@ -140,7 +140,7 @@ struct MapEntry {
   void* c = nullptr;
   int M = 0, N = 0, K = 0, ldc = 0;
   int b_rows = 0;   // rows of B's box: B rows one CTA loads per MMA column block
-  bool c_f32 = false;  // C holds fp32 (fused epilogue output type)
+  int c_type = 0;   // C element type (fused epilogue output type, B200GEMM_OUT_*)
   uint64_t last_use = 0;
   CUtensorMap map_a, map_b, map_c;
 };
@@ -277,6 +277,9 @@ double epilogue_cost(const b200gemm_epilogue* epi, int width) {
   if (epi->out_type == B200GEMM_OUT_F32) {
     w512 += 12.0;
     w256 += 4.0;
+  } else if (epi->out_type == B200GEMM_OUT_E4M3) {
+    w512 += 2.0;
+    w256 += 0.5;
   }
   return width == 512 ? w512 : w256 * width / 256.0;
 }
@@ -473,11 +476,11 @@ int schedule_for(b200gemm_t h, uint32_t tiles_m, uint32_t tiles_n, cudaStream_t 
 
 // Tensor maps for one argument tuple, cached in the handle.  Caller holds h->mu.
 int maps_for(b200gemm_t h, int M, int N, int K, const void* A, const void* B, void* C, int ldc,
-             int b_rows, bool c_f32, CUtensorMap* ma, CUtensorMap* mb, CUtensorMap* mc) {
+             int b_rows, int c_type, CUtensorMap* ma, CUtensorMap* mb, CUtensorMap* mc) {
   MapEntry* slot = nullptr;
   for (auto& m : h->maps) {
     if (m.valid && m.a == A && m.b == B && m.c == C && m.M == M && m.N == N && m.K == K &&
-        m.ldc == ldc && m.b_rows == b_rows && m.c_f32 == c_f32) {
+        m.ldc == ldc && m.b_rows == b_rows && m.c_type == c_type) {
       slot = &m;
       break;
     }
@@ -495,15 +498,19 @@ int maps_for(b200gemm_t h, int M, int N, int K, const void* A, const void* B, vo
     const uint64_t k = static_cast<uint64_t>(K);
     // A: 64 x 128 boxes, B: 64 x b_rows boxes (one 128-byte K row per operand
     // row), 128-byte swizzle as the MMA descriptors expect; C: 32 rows of 64
-    // bytes (32 bf16 or 16 fp32 columns), 64-byte swizzle.
+    // bytes (32 bf16 or 16 fp32 columns), 64-byte swizzle.  (e4m3 C is
+    // written with plain stores; its map is encoded but unused.)
+    const bool c_f32 = c_type == B200GEMM_OUT_F32, c_u8 = c_type == B200GEMM_OUT_E4M3;
+    const uint64_t c_esize = c_f32 ? 4 : (c_u8 ? 1 : 2);
     if (!encode_2d(&slot->map_a, A, k, static_cast<uint64_t>(M), k * 2, kBlockK, 128,
                    CU_TENSOR_MAP_SWIZZLE_128B) ||
         !encode_2d(&slot->map_b, B, k, static_cast<uint64_t>(N), k * 2, kBlockK,
                    static_cast<uint32_t>(b_rows), CU_TENSOR_MAP_SWIZZLE_128B) ||
         !encode_2d(&slot->map_c, C, static_cast<uint64_t>(N), static_cast<uint64_t>(M),
-                   static_cast<uint64_t>(ldc) * (c_f32 ? 4 : 2), c_f32 ? kCBoxCols / 2 : kCBoxCols,
+                   static_cast<uint64_t>(ldc) * c_esize, static_cast<uint32_t>(64 / c_esize),
                    kCBoxRows, CU_TENSOR_MAP_SWIZZLE_64B,
-                   c_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16)) {
+                   c_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                         : (c_u8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16))) {
       return B200GEMM_ERR_CUDA;
     }
     slot->a = A;
@@ -514,7 +521,7 @@ int maps_for(b200gemm_t h, int M, int N, int K, const void* A, const void* B, vo
     slot->K = K;
     slot->ldc = ldc;
     slot->b_rows = b_rows;
-    slot->c_f32 = c_f32;
+    slot->c_type = c_type;
     slot->valid = true;
   }
   slot->last_use = ++h->tick;
@@ -722,9 +729,9 @@ int gemm_device(b200gemm_t h, int M, int N, int K, const void* A, const void* B,
                 const b200gemm_epilogue* epi) {
   if (h == nullptr || M < 0 || N < 0 || K < 0) return B200GEMM_ERR_INVALID_ARG;
   const bool fused = epi != nullptr;
-  const bool c_f32 = fused && epi->out_type == B200GEMM_OUT_F32;
+  const int c_type = fused ? epi->out_type : B200GEMM_OUT_BF16;
   if (fused) {
-    if (epi->out_type != B200GEMM_OUT_BF16 && epi->out_type != B200GEMM_OUT_F32)
+    if (c_type != B200GEMM_OUT_BF16 && c_type != B200GEMM_OUT_F32 && c_type != B200GEMM_OUT_E4M3)
       return B200GEMM_ERR_INVALID_ARG;
     if (epi->activation < B200GEMM_ACT_NONE || epi->activation > B200GEMM_ACT_SILU)
       return B200GEMM_ERR_INVALID_ARG;
@@ -734,7 +741,9 @@ int gemm_device(b200gemm_t h, int M, int N, int K, const void* A, const void* B,
   }
   if (M == 0 || N == 0) return B200GEMM_OK;
   if (C == nullptr || (K > 0 && (A == nullptr || B == nullptr))) return B200GEMM_ERR_INVALID_ARG;
-  if (ldc < N || (ldc % (c_f32 ? 4 : 8)) != 0 || (K % 8) != 0) return B200GEMM_ERR_UNSUPPORTED;
+  // C rows start on 16-byte boundaries: ldc a multiple of 16 bytes.
+  const int ldc_group = c_type == B200GEMM_OUT_F32 ? 4 : (c_type == B200GEMM_OUT_E4M3 ? 16 : 8);
+  if (ldc < N || (ldc % ldc_group) != 0 || (K % 8) != 0) return B200GEMM_ERR_UNSUPPORTED;
   if (fused && K == 0) return B200GEMM_ERR_UNSUPPORTED;  // the kernel needs one K block
   if (!aligned16(C) || (K > 0 && (!aligned16(A) || !aligned16(B)))) return B200GEMM_ERR_UNSUPPORTED;
   const uint32_t tiles_m = static_cast<uint32_t>((M + kTileM - 1) / kTileM);
@@ -773,7 +782,7 @@ int gemm_device(b200gemm_t h, int M, int N, int K, const void* A, const void* B,
     tiles_n = static_cast<uint32_t>((N + width - 1) / width);
     int rc = schedule_for(h, tiles_m, tiles_n, stream, &sched);
     if (rc != B200GEMM_OK) return rc;
-    rc = maps_for(h, M, N, K, A, B, C, ldc, b_box_rows(width), c_f32, &ma, &mb, &mc);
+    rc = maps_for(h, M, N, K, A, B, C, ldc, b_box_rows(width), c_type, &ma, &mb, &mc);
     if (rc != B200GEMM_OK) return rc;
     timeout_ns = h->timeout_ns;
   }
@@ -795,9 +804,10 @@ int gemm_device(b200gemm_t h, int M, int N, int K, const void* A, const void* B,
 
   p.epi_flags = 0;
   p.act = B200GEMM_ACT_NONE;
-  p.out_f32 = c_f32 ? 1 : 0;
+  p.out_type = c_type;
   p.alpha = 1.0f;
   p.beta = 0.0f;
+  p.out_scale = 1.0f;
   p.bias = nullptr;
   p.residual = nullptr;
   p.ldr = 0;
@@ -809,6 +819,7 @@ int gemm_device(b200gemm_t h, int M, int N, int K, const void* A, const void* B,
     p.bias = static_cast<const uint16_t*>(epi->bias);
     p.residual = static_cast<const uint16_t*>(epi->residual);
     p.ldr = epi->ldr;
+    p.out_scale = epi->out_scale == 0.0f ? 1.0f : epi->out_scale;
   }
 
   const int max_clusters = fused ? h->clusters_epi[width_index(width)] : h->clusters_w[width_index(width)];

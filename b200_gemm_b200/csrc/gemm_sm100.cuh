@@ -91,11 +91,12 @@ struct GemmParams {
   unsigned int* tail_counters;  // [tail tile][CTA of the pair], zero between launches
   // Fused epilogue (instances with Cfg::kEpi only), per element in fp32:
   //   D = act(alpha * acc + bias[col]) + beta * residual[row][col]
-  // then rounded to bf16 (RNE) or stored as fp32 (out_f32).
+  // then rounded to bf16 (RNE), stored as fp32, or scaled by out_scale and
+  // rounded to fp8 e4m3 (RNE, saturating), per out_type.
   uint32_t epi_flags;          // kEpiBias | kEpiResidual
   int act;                     // kAct*
-  int out_f32;                 // 1: C holds fp32, ldc in fp32 elements
-  float alpha, beta;
+  int out_type;                // kOutBf16, kOutF32 (ldc in fp32), kOutE4m3 (ldc in bytes)
+  float alpha, beta, out_scale;
   const uint16_t* bias;        // bf16[N]
   const uint16_t* residual;    // bf16, row pitch ldr elements
   long long ldr;
@@ -104,6 +105,7 @@ struct GemmParams {
 constexpr uint32_t kEpiBias = 1u;
 constexpr uint32_t kEpiResidual = 2u;
 constexpr int kActNone = 0, kActRelu = 1, kActGelu = 2, kActGeluTanh = 3, kActSilu = 4;
+constexpr int kOutBf16 = 0, kOutF32 = 1, kOutE4m3 = 2;
 
 // One work unit of a CTA pair: a tile and a K range; slot >= 0 marks a K
 // slice of a split tile (its index among the tail units).
@@ -328,16 +330,33 @@ __device__ __forceinline__ void epi_load_residual(const GemmParams& p, int r, in
   }
 }
 
+// One lane's 32 e4m3 bytes (8 words, column col + 4i + b in byte b of
+// word i) to row r of C, straight from registers: two 16-byte stores when
+// the chunk is whole (rows start 16-byte aligned: ldc % 16 == 0), else one
+// byte per column inside N.
+__device__ __forceinline__ void store_e4m3_row(const uint32_t (&q)[8], int r, int col, const GemmParams& p) {
+  if (r >= p.M || col >= p.N) return;
+  uint8_t* dst = reinterpret_cast<uint8_t*>(p.C) + static_cast<long long>(r) * p.ldc + col;
+  if (col + 32 <= p.N) {
+    ptx::st_global_v4(dst, q[0], q[1], q[2], q[3]);
+    ptx::st_global_v4(dst + 16, q[4], q[5], q[6], q[7]);
+  } else {
+#pragma unroll
+    for (int k = 0; k < 32; ++k)
+      if (col + k < p.N) dst[k] = static_cast<uint8_t>(q[k >> 2] >> (8 * (k & 3)));
+  }
+}
+
 // The fused epilogue on one lane's 32 accumulators (chunk `c` of the warp's
 // column block), in place, fp32 throughout:
 //   D = act(alpha * acc + bias[col]) + beta * residual[r][col].
 // GELU is 0.5 x (1 + erf(x / sqrt 2)) or its tanh form
 // 0.5 x (1 + tanh(sqrt(2 / pi) (x + 0.044715 x^3))) (Hendrycks & Gimpel);
 // SiLU is x / (1 + e^-x).  For fp32 output the transcendentals are CUDA's
-// erff / tanhf / expf; for bf16 output, whose spacing (2^-8 relative) is far
-// coarser than their error, tanh and the reciprocal are the hardware
-// approximations (tanh.approx, rcp.approx) and e^x is __expf.  erf is erff
-// for both.
+// erff / tanhf / expf; for bf16 and e4m3 output, whose spacing (2^-8 and
+// 2^-4 relative) is far coarser than their error, tanh and the reciprocal are
+// the hardware approximations (tanh.approx, rcp.approx) and e^x is __expf.
+// erf is erff for all.
 __device__ __forceinline__ void apply_epilogue(uint32_t (&v)[32], int c, const uint32_t (&bias_w)[4],
                                                const uint32_t (&res_w)[16], const GemmParams& p) {
   float d[32];
@@ -352,7 +371,7 @@ __device__ __forceinline__ void apply_epilogue(uint32_t (&v)[32], int c, const u
       d[2 * q + 1] += bf16_hi(b);
     }
   }
-  const bool fast = p.out_f32 == 0;
+  const bool fast = p.out_type != kOutF32;
   switch (p.act) {
     case kActRelu:
 #pragma unroll
@@ -620,7 +639,16 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
             uint32_t v[32];
             tmem_chunk(c, v);
             apply_epilogue(v, c, bias_w, cur, p);
-            if (p.out_f32) {
+            if (p.out_type == kOutE4m3) {
+              uint32_t q8[8];
+#pragma unroll
+              for (int i = 0; i < 8; ++i)
+                q8[i] = ptx::pack_e4m3x4(p.out_scale * __uint_as_float(v[4 * i]),
+                                         p.out_scale * __uint_as_float(v[4 * i + 1]),
+                                         p.out_scale * __uint_as_float(v[4 * i + 2]),
+                                         p.out_scale * __uint_as_float(v[4 * i + 3]));
+              store_e4m3_row(q8, row + static_cast<int>(lane), col0 + c * kCBoxCols, p);
+            } else if (p.out_type == kOutF32) {
               uint32_t lo[16], hi[16];
 #pragma unroll
               for (int i = 0; i < 16; ++i) {

@@ -350,6 +350,15 @@ __device__ __forceinline__ uint32_t pack_bf16x2(uint32_t lo_f32, uint32_t hi_f32
   return r;
 }
 
+// Four fp32 values -> four fp8 e4m3 bytes (RNE, saturated to +-448; NaN
+// stays NaN), x0 in the lowest byte.
+__device__ __forceinline__ uint32_t pack_e4m3x4(float x0, float x1, float x2, float x3) {
+  uint16_t lo, hi;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(lo) : "f"(x1), "f"(x0));
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(hi) : "f"(x3), "f"(x2));
+  return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+}
+
 // 16-byte store into another CTA's shared memory (shared::cluster address)
 // whose completion is counted, in bytes, on an mbarrier of that CTA.
 __device__ __forceinline__ void st_async_v4(uint32_t cluster_addr, uint32_t cluster_bar, uint32_t a,

@@ -56,8 +56,9 @@ int b200gemm_bf16_nt(b200gemm_t handle, int M, int N, int K, const void* A, cons
 /* Fused epilogue, applied per element in fp32 to the accumulator before C is
  * written (the ops around an MLP projection, without a second pass over C):
  *     D[i][j] = act(alpha * (A . B^T)[i][j] + bias[j]) + beta * residual[i][j]
- * then C[i][j] = D[i][j] rounded to bf16 (RNE) or stored as fp32.  A NULL
- * bias or residual drops that term.  No counterpart in the reference, whose
+ * then C[i][j] = D[i][j] rounded to bf16 (RNE), stored as fp32, or scaled by
+ * out_scale and rounded to fp8 e4m3 (OCP FP8 E4M3: RNE, saturating to
+ * +-448).  A NULL bias or residual drops that term.  No counterpart in the reference, whose
  * epilogue only rounds the accumulator to bf16 (matmul_1.cuh:293-295). */
 #define B200GEMM_ACT_NONE 0
 #define B200GEMM_ACT_RELU 1       /* max(x, 0)                                   */
@@ -66,6 +67,7 @@ int b200gemm_bf16_nt(b200gemm_t handle, int M, int N, int K, const void* A, cons
 #define B200GEMM_ACT_SILU 4       /* x / (1 + exp(-x))                           */
 #define B200GEMM_OUT_BF16 0
 #define B200GEMM_OUT_F32 1
+#define B200GEMM_OUT_E4M3 2
 typedef struct b200gemm_epilogue {
   float alpha;           /* scale of A . B^T                                     */
   float beta;            /* scale of the residual                                */
@@ -74,9 +76,10 @@ typedef struct b200gemm_epilogue {
   int ldr;               /* residual pitch in elements: ldr >= N, ldr % 8 == 0,  */
                          /* residual 16-byte aligned                             */
   int activation;        /* B200GEMM_ACT_*                                       */
-  int out_type;          /* B200GEMM_OUT_BF16 or B200GEMM_OUT_F32 (C holds fp32, */
-                         /* ldc in fp32 elements, ldc % 4 == 0)                  */
-  int reserved;          /* set to 0                                             */
+  int out_type;          /* B200GEMM_OUT_BF16, B200GEMM_OUT_F32 (C holds fp32,   */
+                         /* ldc in fp32 elements, ldc % 4 == 0) or               */
+                         /* B200GEMM_OUT_E4M3 (C holds bytes, ldc % 16 == 0)     */
+  float out_scale;       /* e4m3 output: C = e4m3(out_scale * D); 0 means 1      */
 } b200gemm_epilogue;
 
 /* C = epilogue(A . B^T) with the epilogue above; epi == NULL is exactly

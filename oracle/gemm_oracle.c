@@ -265,3 +265,48 @@ void oracle_epilogue_sampled(double* vals, const int* rows, const int* cols, siz
   for (size_t s = 0; s < count; ++s)
     vals[s] = epi_one(vals[s], rows[s], cols[s], alpha, bias, act, R, ldr, beta);
 }
+
+/* ----------------------------------------------------- fp8 e4m3 (OCP FP8)
+ * E4M3 "fn": 1 sign, 4 exponent (bias 7), 3 mantissa bits, no infinities,
+ * S.1111.111 is NaN, largest finite 448 = 1.75 * 2^8, smallest normal 2^-6,
+ * subnormal step 2^-9.  Encoding rounds to nearest, ties to even, and
+ * saturates anything at or beyond 448 in magnitude to +-448 (the library's
+ * fp8 output uses cvt.rn.satfinite, which does the same); NaN -> 0x7F. */
+uint8_t oracle_f64_to_e4m3_one(double x) {
+  if (isnan(x)) return 0x7F;
+  const uint8_t sign = signbit(x) ? 0x80 : 0x00;
+  const double a = fabs(x);
+  if (a >= 448.0) return sign | 0x7E;
+  if (a == 0.0) return sign;
+  int e;
+  frexp(a, &e);                 /* a = f * 2^e, f in [0.5, 1) */
+  int E = e - 1;                /* exponent of the leading bit */
+  if (E < -6) E = -6;           /* subnormal range shares the 2^-9 quantum */
+  const double q = ldexp(1.0, E - 3);
+  const double v = nearbyint(a / q) * q;   /* a / q is exact (power-of-two scale) */
+  if (v >= 448.0) return sign | 0x7E;      /* unreachable for a < 448, kept for safety */
+  if (v == 0.0) return sign;
+  int ev;
+  frexp(v, &ev);
+  const int Ev = ev - 1;
+  if (Ev < -6) return sign | (uint8_t)(v / ldexp(1.0, -9));            /* subnormal */
+  const int mant = (int)(v / ldexp(1.0, Ev - 3)) - 8;
+  return sign | (uint8_t)((Ev + 7) << 3) | (uint8_t)mant;
+}
+
+double oracle_e4m3_to_f64_one(uint8_t b) {
+  const int s = b >> 7, e = (b >> 3) & 15, m = b & 7;
+  double v;
+  if (e == 15 && m == 7) return NAN;
+  if (e == 0) v = ldexp((double)m, -9);
+  else v = ldexp(1.0 + m / 8.0, e - 7);
+  return s ? -v : v;
+}
+
+void oracle_f64_to_e4m3(const double* in, uint8_t* out, size_t n) {
+  for (size_t i = 0; i < n; ++i) out[i] = oracle_f64_to_e4m3_one(in[i]);
+}
+
+void oracle_e4m3_to_f64(const uint8_t* in, double* out, size_t n) {
+  for (size_t i = 0; i < n; ++i) out[i] = oracle_e4m3_to_f64_one(in[i]);
+}

@@ -67,6 +67,9 @@ def lib():
                                               c_int, c_double]
             L.oracle_epilogue_sampled.argtypes = [_f64p, _i32p, _i32p, c_size, c_double, vp, c_int,
                                                   vp, c_int, c_double]
+            _u8p = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
+            L.oracle_f64_to_e4m3.argtypes = [_f64p, _u8p, c_size]
+            L.oracle_e4m3_to_f64.argtypes = [_u8p, _f64p, c_size]
             _lib = L
         return _lib
 
@@ -177,6 +180,28 @@ def epilogue_sampled(vals, rows, cols, alpha=1.0, bias=None, act="none", residua
     lib().oracle_epilogue_sampled(out, rows, cols, out.shape[0], float(alpha), bp, ACTIVATIONS[act],
                                   rp, ldr, float(beta))
     return out
+
+
+def f64_to_e4m3(x) -> np.ndarray:
+    """fp64 -> OCP FP8 E4M3 bytes (RNE, saturating to +-448)."""
+    x = np.ascontiguousarray(x, dtype=np.float64)
+    out = np.empty(x.shape, dtype=np.uint8)
+    lib().oracle_f64_to_e4m3(x.reshape(-1), out.reshape(-1), x.size)
+    return out
+
+
+def e4m3_to_f64(b) -> np.ndarray:
+    b = np.ascontiguousarray(b, dtype=np.uint8)
+    out = np.empty(b.shape, dtype=np.float64)
+    lib().oracle_e4m3_to_f64(b.reshape(-1), out.reshape(-1), b.size)
+    return out
+
+
+def e4m3_ulp(x) -> np.ndarray:
+    """Spacing of e4m3 values around |x| (2^-9 in the subnormal range)."""
+    a = np.abs(np.asarray(x, dtype=np.float64))
+    e = np.floor(np.log2(np.maximum(a, 2.0 ** -6)))
+    return np.ldexp(1.0, (np.minimum(e, 8) - 3).astype(np.int64))
 
 
 def num_cpus() -> int:

@@ -105,6 +105,68 @@ def test_large_activation_range(gpu_handle, oracle_mod):
         _case(gpu_handle, oracle_mod, 256, 256, 136, act, True, False, 8.0, 1.0, torch.bfloat16, seed=5)
 
 
+def _e4m3_case(h, oracle_mod, M, N, K, act, use_bias, use_res, scale, seed, width=0):
+    A_bits, B_bits = data.host_operands(M, N, K, "normal", seed=seed)
+    bias_bits = _rand_bits((N,), seed + 1) if use_bias else None
+    res_bits = _rand_bits((M, N), seed + 2) if use_res else None
+    A, B = _dev(A_bits), _dev(B_bits)
+    bias = _dev(bias_bits) if use_bias else None
+    res = None
+    if use_res:  # rows 16-byte aligned: pad the pitch to a multiple of 8
+        full = torch.zeros(M, 8 * ((N + 7) // 8), dtype=torch.bfloat16, device="cuda")
+        full[:, :N] = _dev(res_bits)
+        res = full[:, :N]
+    ldc = 16 * ((N + 15) // 16) + 16
+    Cbuf = torch.full((M + 32, ldc), 0x7F, dtype=torch.uint8, device="cuda")  # 0x7F = NaN
+    out = Cbuf.view(torch.float8_e4m3fn)[:M, :N]
+    h.set_tile_width(width)
+    try:
+        h.bf16_nt_epilogue(A, B, bias=bias, activation=act, residual=res, alpha=1.0, beta=1.0,
+                           out=out, out_scale=scale)
+    finally:
+        h.set_tile_width(0)
+    torch.cuda.synchronize()
+    assert h.last_device_status()[0] == 0
+    allc = Cbuf.cpu().numpy()
+    assert np.all(allc[M:] == 0x7F) and np.all(allc[:M, N:] == 0x7F), "write outside C"
+    ref = scale * oracle_mod.epilogue_f64(oracle_mod.gemm_f64(A_bits, B_bits), bias=bias_bits, act=act,
+                                          residual=res_bits, beta=1.0)
+    got = oracle_mod.e4m3_to_f64(allc[:M, :N])
+    sat = np.abs(ref) >= 448.0
+    assert np.all(got[sat] == np.sign(ref[sat]) * 448.0)
+    # within one e4m3 step of the exact value (RNE of a value within fp32
+    # accumulation error of it)
+    ok = np.abs(got - ref) <= oracle_mod.e4m3_ulp(ref)
+    assert ok[~sat].all(), float(np.abs(got - ref)[~sat].max())
+    return A, B
+
+
+@pytest.mark.parametrize("act,use_bias,use_res", [("none", False, False), ("gelu_tanh", True, False),
+                                                  ("silu", True, True), ("relu", False, True)])
+@pytest.mark.parametrize("width", [512, 224])
+def test_epilogue_e4m3(gpu_handle, oracle_mod, act, use_bias, use_res, width):
+    # ragged N (not a multiple of 16 or 32); scale spreads values over the
+    # e4m3 range, some past 448 (saturation)
+    _e4m3_case(gpu_handle, oracle_mod, 300, 203, 136, act, use_bias, use_res, 16.0, seed=31, width=width)
+
+
+def test_epilogue_e4m3_bit_exact_vs_fp32(gpu_handle, oracle_mod):
+    """e4m3 output = the oracle's RNE-saturating encoding of (out_scale x the
+    fp32 output) bit for bit (ReLU: no transcendental): pins the device
+    conversion to the oracle's codec."""
+    h = gpu_handle
+    M, N, K = 512, 768, 256
+    A, B = data.device_operands(M, N, K, "normal", seed=17)
+    scale = 3.0
+    C32 = h.bf16_nt_epilogue(A, B, activation="relu", out_dtype=torch.float32)
+    C8 = h.bf16_nt_epilogue(A, B, activation="relu", out_dtype=torch.float8_e4m3fn, out_scale=scale)
+    torch.cuda.synchronize()
+    x = (C32.cpu().numpy().astype(np.float32) * np.float32(scale)).astype(np.float64)
+    want = oracle_mod.f64_to_e4m3(x)
+    got = C8.contiguous().view(torch.uint8).cpu().numpy()
+    assert np.array_equal(got, want)
+
+
 @pytest.mark.parametrize("width", [512, 256, 224])
 def test_identity_epilogue_bit_exact(gpu_handle, width):
     """No terms: the fused instance writes exactly what the plain GEMM writes;
@@ -184,6 +246,9 @@ def test_epilogue_argument_errors(gpu_handle):
     assert call(_lib.Epilogue(alpha=1.0), k=0) == _lib.ERR_UNSUPPORTED
     assert call(_lib.Epilogue(alpha=1.0, out_type=_lib.OUT_F32), c=Cf, ldc=N + 2) == _lib.ERR_UNSUPPORTED
     assert call(_lib.Epilogue(alpha=1.0, out_type=_lib.OUT_F32), c=Cf, ldc=N + 4) == _lib.OK
+    C8 = torch.empty(M, N + 16, dtype=torch.uint8, device="cuda")
+    assert call(_lib.Epilogue(alpha=1.0, out_type=_lib.OUT_E4M3), c=C8, ldc=N + 8) == _lib.ERR_UNSUPPORTED
+    assert call(_lib.Epilogue(alpha=1.0, out_type=_lib.OUT_E4M3, out_scale=2.0), c=C8, ldc=N + 16) == _lib.OK
     # NULL epilogue = the plain GEMM
     assert L.b200gemm_bf16_nt_epilogue(h._h, M, N, K, A.data_ptr(), B.data_ptr(), C.data_ptr(), N,
                                        None, s) == _lib.OK

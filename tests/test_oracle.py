@@ -146,3 +146,25 @@ def test_epilogue_restatement(oracle_mod, act):
     assert np.allclose(got_s, want[rows, cols], rtol=1e-12, atol=1e-12)
     # no bias, no residual: only the scale and the activation
     assert np.allclose(o.epilogue_f64(S, alpha=alpha, act=act), f(alpha * S), rtol=1e-12, atol=1e-12)
+
+
+def test_e4m3_codec(oracle_mod):
+    """The oracle's fp8 e4m3 encoder (RNE, saturating) against torch's
+    float8_e4m3fn conversion on in-range values, exact round trips, and the
+    saturation / NaN / subnormal edges."""
+    torch = pytest.importorskip("torch")
+    o = oracle_mod
+    rng = np.random.Generator(np.random.PCG64(8))
+    x = (rng.standard_normal(100000) * np.exp2(rng.uniform(-12, 10, 100000))).astype(np.float32)
+    x = x[np.abs(x) < 448].astype(np.float64)
+    want = torch.from_numpy(x.astype(np.float32)).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    assert np.array_equal(o.f64_to_e4m3(x), want)
+    every = np.arange(256, dtype=np.uint8)
+    vals = o.e4m3_to_f64(every)
+    finite = ~np.isnan(vals)
+    assert np.sum(~finite) == 2  # 0x7F and 0xFF
+    assert np.array_equal(o.f64_to_e4m3(vals[finite])[vals[finite] != 0],
+                          every[finite][vals[finite] != 0])
+    edge = np.array([448.0, 463.9, 464.0, 1e30, -1e30, 2.0 ** -9, 2.0 ** -10, 3 * 2.0 ** -11, np.nan])
+    assert list(o.f64_to_e4m3(edge)) == [0x7E, 0x7E, 0x7E, 0x7E, 0xFE, 0x01, 0x00, 0x01, 0x7F]
+    assert np.allclose(o.e4m3_ulp([1.0, 1.9, 448.0, 1e-3]), [0.125, 0.125, 32.0, 2.0 ** -9])
