@@ -242,6 +242,19 @@ def time_epilogue(gemm, torch, A, B, C, args, flush, stream, dev, barrier, flops
     return res
 
 
+def launch_shape(gemm, M, N, K, info, library_arm):
+    """Grid geometry of our kernel for this shape (what the library's plan says)."""
+    if library_arm:
+        return None
+    plan = gemm.plan(M, N, K)
+    if plan["kernel"] == "small_m":
+        split = plan["small_m_split"]
+        return dict(info, kernel="small_m", ctas=plan["tiles"] * 2 * split, threads_per_cta=192,
+                    cluster=2 * split)
+    return dict(info, kernel="tiled", clusters=plan["clusters"], tiles=plan["tiles"],
+                threads_per_cta=320 if plan["tile_width"] == 512 else 192, cluster=2)
+
+
 def roofline(w, M, N, K, ms_per_launch, peaks, peak_kind, traffic):
     """Roofline entry for the dominant kernel.  Tensor-bound shapes report
     TFLOP/s against the measured bf16 GEMM peak; HBM-bound shapes (small M)
@@ -516,7 +529,7 @@ def run_ours(args, w):
                              ("operands %.0f MB < 2x L2: 256 MB L2 flush before each step, "
                               "per-step CUDA events" % (operand_bytes / 1e6))},
             "gpu_launches": 0 if library_arm else args.steps,
-            "launch": dict(info, threads_per_cta=192, cluster=2),
+            "launch": launch_shape(gemm, M, Nl, K, info, library_arm),
             "roofline": roofline(w, M, Nl, K, ms / args.steps, peaks, peak_kind, traffic),
             "clocks": clocks.summary(),
         }
@@ -525,7 +538,11 @@ def run_ours(args, w):
             result["impl"] = "cublaslt"
             result["tile_width"] = None
         else:
-            result["tile_width"] = gemm.tile_width_for(M, Nl, K)
+            plan = gemm.plan(M, Nl, K)
+            result["kernel"] = plan["kernel"]
+            result["tile_width"] = plan["tile_width"] if plan["kernel"] == "tiled" else None
+            if plan["kernel"] == "small_m":
+                result["small_m_split"] = plan["small_m_split"]
         if not args.no_cpu_baseline and not library_arm:
             result["cpu_baseline"] = cpu_baseline(w, args.seed, args.cpu_seconds)
     gemm.close()
