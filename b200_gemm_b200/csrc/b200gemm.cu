@@ -23,7 +23,10 @@ namespace b200gemm {
 #define B200GEMM_STAGES_N256 6
 #endif
 #ifndef B200GEMM_STAGES_N512
-#define B200GEMM_STAGES_N512 4
+#define B200GEMM_STAGES_N512 3
+#endif
+#ifndef B200GEMM_EPIWARPS_N512
+#define B200GEMM_EPIWARPS_N512 16
 #endif
 #ifndef B200GEMM_DEFAULT_ORDER
 #define B200GEMM_DEFAULT_ORDER 1
@@ -32,7 +35,9 @@ namespace b200gemm {
 #define B200GEMM_DEFAULT_BAND 16
 #endif
 using CfgN256 = GemmCfg<B200GEMM_STAGES_N256, 1>;  // 256 x 256 tiles, overlapped epilogue
-using CfgN512 = GemmCfg<B200GEMM_STAGES_N512, 2>;  // 256 x 512 tiles, shared A stage
+// 256 x 512 tiles, shared A stage; 16 epilogue warps drain the single
+// 512-column accumulator (3 stages leave room for their staging buffers).
+using CfgN512 = GemmCfg<B200GEMM_STAGES_N512, 2, 256, false, B200GEMM_EPIWARPS_N512>;
 // Narrower tiles for N that 256 does not divide into full waves (e.g. an
 // N-sharded projection with N = 1792 = 8 x 224); more stages fit because each
 // stage holds fewer B rows.
@@ -41,7 +46,7 @@ using CfgN192 = GemmCfg<7, 1, 192>;
 using CfgN128 = GemmCfg<8, 1, 128>;
 // The same five widths with the fused epilogue compiled in.
 using CfgE256 = GemmCfg<B200GEMM_STAGES_N256, 1, 256, true>;
-using CfgE512 = GemmCfg<B200GEMM_STAGES_N512, 2, 256, true>;
+using CfgE512 = GemmCfg<4, 2, 256, true>;  // 8 epilogue warps: the fused math needs their registers
 using CfgE224 = GemmCfg<6, 1, 224, true>;
 using CfgE192 = GemmCfg<7, 1, 192, true>;
 using CfgE128 = GemmCfg<8, 1, 128, true>;
@@ -539,6 +544,12 @@ namespace {
 
 bool tail_split_enabled_for(const b200gemm_handle* h) { return h->tail_split_enabled; }
 
+// Instances that carry the K-split tail (GemmCfg::kTailSplit): the plain
+// ones except the 512-wide, whose 16 epilogue warps leave it no registers.
+bool tail_split_width(int width, bool fused) {
+  return !fused && (width == 512 ? CfgN512::kTailSplit : true);
+}
+
 // Tile width (one of kWidths) a call on this handle will use: the cheapest
 // by tile_plan_cost (with the fused epilogue's cost when `epi` is given), the
 // earlier entry of kWidths on a tie.
@@ -826,7 +837,9 @@ int gemm_device(b200gemm_t h, int M, int N, int K, const void* A, const void* B,
   const int clusters = p.num_tiles < max_clusters ? p.num_tiles : max_clusters;
   // Split the last partial wave along K when it leaves clusters idle (plain
   // epilogue only: the split tiles' reduction writes bf16 directly).
-  const int sk = (tail_split_enabled_for(h) && !fused) ? tail_split_for(p.num_tiles, clusters, p.num_kb) : 1;
+  const int sk = (tail_split_enabled_for(h) && tail_split_width(width, fused))
+                     ? tail_split_for(p.num_tiles, clusters, p.num_kb)
+                     : 1;
   p.tail_start = p.num_tiles;
   p.tail_split = 1;
   p.tail_kb = p.num_kb;
@@ -894,7 +907,7 @@ extern "C" int b200gemm_plan(b200gemm_t h, int M, int N, int K, int* plan) {
   plan[1] = width;
   plan[2] = tiles;
   plan[3] = clusters;
-  plan[4] = h->tail_split_enabled ? tail_split_for(tiles, clusters, num_kb) : 1;
+  plan[4] = (h->tail_split_enabled && tail_split_width(width, false)) ? tail_split_for(tiles, clusters, num_kb) : 1;
   return B200GEMM_OK;
 }
 

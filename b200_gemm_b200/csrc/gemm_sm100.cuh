@@ -39,6 +39,9 @@
 #ifndef B200GEMM_L2_POLICY_B
 #define B200GEMM_L2_POLICY_B 1
 #endif
+#ifndef B200GEMM_CBUFS_N512
+#define B200GEMM_CBUFS_N512 2
+#endif
 
 
 namespace b200gemm {
@@ -144,7 +147,12 @@ __device__ __forceinline__ WorkUnit unit_at(const GemmParams& p, uint32_t u) {
 //           so the tile width can divide N and fill the last wave.
 //   EPI:    fused epilogue (bias, activation, residual, fp32 output) compiled
 //           in; the plain instances carry none of its code.
-template <int STAGES, int NB, int MN = 256, bool EPI = false>
+//   EW:     epilogue warps (a multiple of 4; warp w reads TMEM lanes
+//           32 (w % 4) ..); each drains kTileN * 4 / EW columns of its lanes.
+//           More warps drain a single (non double-buffered) accumulator
+//           sooner: every warp's chunks run as one serial chain of TMEM load,
+//           staging and TMA store.
+template <int STAGES, int NB, int MN = 256, bool EPI = false, int EW = 4 * NB>
 struct GemmCfg {
   static_assert(NB == 1 || NB == 2, "one or two MMA column blocks per tile");
   static_assert(MN % 32 == 0 && MN >= 64 && MN <= 256 && (NB == 1 || MN == 256), "MMA width");
@@ -154,16 +162,26 @@ struct GemmCfg {
   static constexpr int kMmaN = MN;                       // columns per tcgen05.mma
   static constexpr int kBRows = MN / 2;                  // B rows per CTA per column block
   static constexpr int kBlockBytesB = kBRows * kBlockK * 2;
-  static constexpr int kChunks = MN / kCBoxCols;         // 32-column epilogue chunks per block
+  static constexpr int kChunks = MN / kCBoxCols;         // 32-column chunks per MMA column block
   static constexpr int kTileN = MN * NB;
   static constexpr int kAccBufs = NB == 1 ? 2 : 1;
   static constexpr int kAccStride = 256;                 // TMEM column of accumulator 1
   // kind::f16: D f32, A = B = bf16, K-major, M = 256 (pair), N = MN.
   static constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) |
                                      (static_cast<uint32_t>(MN >> 3) << 17) | ((kTileM >> 4) << 24);
-  static constexpr int kEpiWarps = 4 * NB;
+  static constexpr int kEpiWarps = EW;
+  static constexpr int kColsPerWarp = MN * NB * 4 / EW;       // tile columns one epilogue warp drains
+  static constexpr int kWarpChunks = kColsPerWarp / kCBoxCols;
+  static_assert(EW % 4 == 0 && kColsPerWarp % kCBoxCols == 0 && kWarpChunks >= 1, "epilogue warps");
+  // K-split tail units (fp32 partials + reduction) are compiled into the
+  // plain instances with at most 8 epilogue warps (more warps leave too few
+  // registers per thread for the reduction); the host splits no other.
+  static constexpr bool kTailSplit = !EPI && EW <= 8;
   static constexpr int kThreads = 64 + 32 * kEpiWarps;
-  static constexpr int kCBufs = 2;   // staging buffers per epilogue warp
+  // Staging buffers per epilogue warp: a chunk's buffer is free once the
+  // TMA store issued kCBufs chunks earlier has read it (about a microsecond),
+  // so more buffers let a warp drain its accumulator faster.
+  static constexpr int kCBufs = NB == 2 ? B200GEMM_CBUFS_N512 : 2;
   static constexpr int kStageBytesB = kBlockBytesB * NB;
   static constexpr uint32_t kTxBytes = 2 * (kStageBytesA + kStageBytesB);  // both CTAs
   // shared memory layout (offsets from a 1024-byte aligned base)
@@ -571,7 +589,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
     // ------------------------------------------------------------ epilogue
     const uint32_t e = warp - 2u;         // epilogue warp index
     const uint32_t quarter = warp & 3u;   // TMEM lanes this warp may access
-    const uint32_t nblk = e >> 2;         // which 256-column block of the tile
+    const uint32_t nblk = e >> 2;         // which slice of kColsPerWarp columns of the tile
     const uint32_t cstage0 = sC + e * Cfg::kCBufs * kCStageBytes;
     const uint32_t tempty_leader0 = ptx::mapa(tempty0, 0);
     uint32_t acc = 0, acc_phase = 0, cbuf = 0;
@@ -583,7 +601,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
       const uint32_t tile = cur.tile;
       const int row = static_cast<int>(tile >> 16) * kTileM + static_cast<int>(rank) * 128 +
                       static_cast<int>(quarter) * 32;
-      const int col0 = static_cast<int>(tile & 0xFFFFu) * Cfg::kTileN + static_cast<int>(nblk) * Cfg::kMmaN;
+      const int col0 = static_cast<int>(tile & 0xFFFFu) * Cfg::kTileN + static_cast<int>(nblk) * Cfg::kColsPerWarp;
       [[maybe_unused]] uint32_t bias_w[4];
       [[maybe_unused]] uint32_t res_w[16];
       if constexpr (Cfg::kEpi) {
@@ -593,10 +611,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
           // the MMAs run, so the per-chunk loads below wait on L2, not DRAM.
           const uint16_t* src = p.residual + static_cast<long long>(r) * p.ldr;
 #pragma unroll
-          for (int b = 1; b < (Cfg::kMmaN * 2 + 127) / 128; ++b)
+          for (int b = 1; b < (Cfg::kColsPerWarp * 2 + 127) / 128; ++b)
             if (col0 + 64 * b < p.N) ptx::prefetch_l2(src + col0 + 64 * b);
         }
-        epi_load_bias(p, col0, Cfg::kMmaN, lane, bias_w);
+        epi_load_bias(p, col0, Cfg::kColsPerWarp, lane, bias_w);
         epi_load_residual(p, r, col0, res_w);
       }
       // After a timeout (here or in another role) the loop keeps running
@@ -606,7 +624,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
       const bool live = __all_sync(0xFFFFFFFFu, full_ok);  // warp-uniform
       ptx::tc_fence_after();
       const uint32_t t_row =
-          tmem_base + ((quarter * 32u) << 16) + acc * Cfg::kAccStride + nblk * Cfg::kMmaN;
+          tmem_base + ((quarter * 32u) << 16) + acc * Cfg::kAccStride + nblk * Cfg::kColsPerWarp;
       if (cur.slot < 0 && !live) {
         // nothing to do for this tile
       } else if (cur.slot < 0) {
@@ -616,7 +634,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
           ptx::tmem_ld_32x32b_x32(t_row + c * kCBoxCols, v);
           ptx::tmem_wait_ld();
           ptx::reg_fence32(v);
-          if (c == Cfg::kChunks - 1) {
+          if (c == Cfg::kWarpChunks - 1) {
             // This warp's part of the accumulator is in registers: release it.
             ptx::tc_fence_before();
             __syncwarp();
@@ -634,7 +652,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
           // buffers take turns so no register copy waits on those loads.
           uint32_t res_b[16];
           auto chunk = [&](int c, const uint32_t (&cur)[16], uint32_t (&nxt)[16]) {
-            if (c + 1 < Cfg::kChunks)
+            if (c + 1 < Cfg::kWarpChunks)
               epi_load_residual(p, row + static_cast<int>(lane), col0 + (c + 1) * kCBoxCols, nxt);
             uint32_t v[32];
             tmem_chunk(c, v);
@@ -663,19 +681,19 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
             }
           };
 #pragma unroll 1
-          for (int c = 0; c < Cfg::kChunks; c += 2) {
+          for (int c = 0; c < Cfg::kWarpChunks; c += 2) {
             chunk(c, res_w, res_b);
-            if (c + 1 < Cfg::kChunks) chunk(c + 1, res_b, res_w);
+            if (c + 1 < Cfg::kWarpChunks) chunk(c + 1, res_b, res_w);
           }
         } else {
 #pragma unroll 1
-          for (int c = 0; c < Cfg::kChunks; ++c) {
+          for (int c = 0; c < Cfg::kWarpChunks; ++c) {
             uint32_t v[32];
             tmem_chunk(c, v);
             store_bf16(c, v);
           }
         }
-      } else if constexpr (!Cfg::kEpi) {
+      } else if constexpr (Cfg::kTailSplit) {
         // K slice of a split tile.  Partials are laid out so that the 32
         // threads of a warp (32 consecutive rows) touch 512 contiguous bytes
         // per 16-byte column group: [column group][row 0..127] of float4.
@@ -685,14 +703,14 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
         auto part = [&](int slot) { return p.workspace + (static_cast<size_t>(slot) * 2 + rank) * slab; };
         float* mine = part(cur.slot);
 #pragma unroll 1
-        for (int c = 0; c < (live ? Cfg::kChunks : 0); ++c) {
+        for (int c = 0; c < (live ? Cfg::kWarpChunks : 0); ++c) {
           uint32_t v[32];
           ptx::tmem_ld_32x32b_x32(t_row + c * kCBoxCols, v);
           ptx::tmem_wait_ld();
           ptx::reg_fence32(v);
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            const size_t g = static_cast<size_t>((nblk * (Cfg::kChunks) + c) * 8 + j);
+            const size_t g = static_cast<size_t>((nblk * (Cfg::kWarpChunks) + c) * 8 + j);
             ptx::st_global_v4(mine + (g * 128 + i) * 4, v[4 * j], v[4 * j + 1], v[4 * j + 2],
                               v[4 * j + 3]);
           }
@@ -716,7 +734,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
           __threadfence();
           const int first = tile_r * p.tail_split;
 #pragma unroll 1
-          for (int c = 0; c < Cfg::kChunks; ++c) {
+          for (int c = 0; c < Cfg::kWarpChunks; ++c) {
             // Sum the slices in slice order whichever slice arrives last, so
             // the result does not depend on timing; this slice's own partial
             // comes from TMEM at its place in the order.  Two 16-column halves
@@ -740,7 +758,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
 #pragma unroll
                   for (int j = 0; j < 4; ++j) {
                     const size_t g =
-                        static_cast<size_t>((nblk * (Cfg::kChunks) + c) * 8 + hh * 4 + j);
+                        static_cast<size_t>((nblk * (Cfg::kWarpChunks) + c) * 8 + hh * 4 + j);
                     uint32_t x0, x1, x2, x3;
                     ptx::ld_global_cg_v4(other + (g * 128 + i) * 4, x0, x1, x2, x3);
                     x[4 * j] = __uint_as_float(x0);

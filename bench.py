@@ -252,7 +252,7 @@ def launch_shape(gemm, M, N, K, info, library_arm):
         return dict(info, kernel="small_m", ctas=plan["tiles"] * 2 * split, threads_per_cta=192,
                     cluster=2 * split)
     return dict(info, kernel="tiled", clusters=plan["clusters"], tiles=plan["tiles"],
-                threads_per_cta=320 if plan["tile_width"] == 512 else 192, cluster=2)
+                threads_per_cta=576 if plan["tile_width"] == 512 else 192, cluster=2)
 
 
 def roofline(w, M, N, K, ms_per_launch, peaks, peak_kind, traffic):

@@ -23,8 +23,9 @@ def _close(got, ref):
     return bool(((g - r).abs() <= 2.0 ** -7 * (r.abs() + 1.0)).all())
 
 
-# (M, N, K, tile width): last waves of 26, 4 and 34 tiles on 74 clusters
-CASES = [(2560, 2560, 512, 256), (16384, 1792, 1024, 256), (16384, 2048, 2048, 512)]
+# (M, N, K, tile width): last waves of 26, 4 and 8 tiles on 74 clusters
+# (the 512-wide instance carries no K-split tail)
+CASES = [(2560, 2560, 512, 256), (16384, 1792, 1024, 256), (16384, 1792, 2048, 128)]
 
 
 @pytest.mark.parametrize("M,N,K,width", CASES)
@@ -60,3 +61,15 @@ def test_tail_split_parity(gpu_handle, oracle_mod, M, N, K, width):
     ref = oracle_mod.gemm_sampled(A_bits, B_bits, rows, cols)
     got = oracle_mod.bf16_to_f32(_bits(C1)[rows, cols])
     assert oracle_mod.within_tolerance(got, ref).all()
+
+
+def test_no_tail_split_at_width_512(gpu_handle):
+    h = gpu_handle
+    h.set_tile_width(512)
+    h.set_tail_split(True)
+    try:
+        plan = h.plan(16384, 2048, 2048)
+    finally:
+        h.set_tile_width(0)
+        h.set_tail_split(False)
+    assert plan["tile_width"] == 512 and plan["tail_split"] == 1
