@@ -62,3 +62,25 @@ def test_create_without_gpu_reports_no_device():
     h = ctypes.c_void_p()
     assert _lib.load().b200gemm_create(ctypes.byref(h), 0) == _lib.ERR_NO_DEVICE
     assert not h.value
+
+
+def test_python_constants_match_header():
+    """Every #define the Python side mirrors has the header's value."""
+    text = (ROOT / "include" / "b200gemm.h").read_text()
+    defines = {m.group(1): int(m.group(2)) for m in re.finditer(r"#define\s+B200GEMM_(\w+)\s+(\d+)", text)}
+    mirror = {
+        "OK": _lib.OK, "ERR_INVALID_ARG": _lib.ERR_INVALID_ARG, "ERR_UNSUPPORTED": _lib.ERR_UNSUPPORTED,
+        "ERR_CUDA": _lib.ERR_CUDA, "ERR_DEVICE_TIMEOUT": _lib.ERR_DEVICE_TIMEOUT,
+        "ERR_NO_DEVICE": _lib.ERR_NO_DEVICE, "ERR_TOO_LARGE": _lib.ERR_TOO_LARGE,
+        "ORDER_HILBERT": _lib.ORDER_HILBERT, "ORDER_BANDS": _lib.ORDER_BANDS,
+        "ACT_NONE": _lib.ACT_NONE, "ACT_RELU": _lib.ACT_RELU, "ACT_GELU": _lib.ACT_GELU,
+        "ACT_GELU_TANH": _lib.ACT_GELU_TANH, "ACT_SILU": _lib.ACT_SILU,
+        "OUT_BF16": _lib.OUT_BF16, "OUT_F32": _lib.OUT_F32, "OUT_E4M3": _lib.OUT_E4M3,
+    }
+    for name, value in mirror.items():
+        assert defines.get(name) == value, name
+    # struct b200gemm_epilogue field order as the ctypes mirror declares it
+    body = re.search(r"typedef struct b200gemm_epilogue \{(.*?)\} b200gemm_epilogue;", text, re.S).group(1)
+    body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
+    fields = re.findall(r"(\w+);", body)
+    assert fields == [f for f, _ in _lib.Epilogue._fields_]
