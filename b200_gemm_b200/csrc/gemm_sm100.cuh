@@ -42,6 +42,12 @@
 #ifndef B200GEMM_CBUFS_N512
 #define B200GEMM_CBUFS_N512 2
 #endif
+// 256 x 512 tiles: chunks per epilogue warp held in registers (packed bf16)
+// between the TMEM read and the store, so the accumulator is released after
+// fewer store chains.
+#ifndef B200GEMM_HELD_N512
+#define B200GEMM_HELD_N512 3
+#endif
 
 
 namespace b200gemm {
@@ -177,6 +183,11 @@ struct GemmCfg {
   // plain instances with at most 8 epilogue warps (more warps leave too few
   // registers per thread for the reduction); the host splits no other.
   static constexpr bool kTailSplit = !EPI && EW <= 8;
+  // Plain instances with one accumulator: the last kHeldChunks chunks of
+  // each warp are read from TMEM into registers (16 per chunk) after the
+  // others went through the store chain; TMEM is released before those are
+  // stored.
+  static constexpr int kHeldChunks = (!EPI && NB == 2) ? (B200GEMM_HELD_N512 < kWarpChunks ? B200GEMM_HELD_N512 : kWarpChunks) : 0;
   static constexpr int kThreads = 64 + 32 * kEpiWarps;
   // Staging buffers per epilogue warp: a chunk's buffer is free once the
   // TMA store issued kCBufs chunks earlier has read it (about a microsecond),
@@ -685,6 +696,33 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
             chunk(c, res_w, res_b);
             if (c + 1 < Cfg::kWarpChunks) chunk(c + 1, res_b, res_w);
           }
+        } else if constexpr (Cfg::kHeldChunks > 0) {
+          constexpr int kFirst = Cfg::kWarpChunks - Cfg::kHeldChunks;
+#pragma unroll 1
+          for (int c = 0; c < kFirst; ++c) {
+            uint32_t v[32];
+            ptx::tmem_ld_32x32b_x32(t_row + c * kCBoxCols, v);
+            ptx::tmem_wait_ld();
+            ptx::reg_fence32(v);
+            store_bf16(c, v);
+          }
+          uint32_t pk[Cfg::kHeldChunks][16];
+#pragma unroll
+          for (int h = 0; h < Cfg::kHeldChunks; ++h) {
+            uint32_t v[32];
+            ptx::tmem_ld_32x32b_x32(t_row + (kFirst + h) * kCBoxCols, v);
+            ptx::tmem_wait_ld();
+            ptx::reg_fence32(v);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) pk[h][i] = ptx::pack_bf16x2(v[2 * i], v[2 * i + 1]);
+          }
+          // Every TMEM read of this warp is done: release the accumulator.
+          ptx::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive_cluster(tempty_leader0 + 8 * acc);
+#pragma unroll
+          for (int h = 0; h < Cfg::kHeldChunks; ++h)
+            store_c_chunk<Cfg>(pk[h], col0 + (kFirst + h) * kCBoxCols, row, lane, cstage0, cbuf, map_c, p);
         } else {
 #pragma unroll 1
           for (int c = 0; c < Cfg::kWarpChunks; ++c) {
