@@ -47,13 +47,14 @@ WORKLOADS = {
 METRIC = "bf16 GEMM TFLOPS @8192^3 (1 GPU) + N-GPU aggregate"
 L2_BYTES = 126 * 1024 * 1024
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+SPEC_PEAKS = {"hbm_gbs": 8000.0, "bf16_tflops": 2250.0}  # public dense figures, for context
 
 
 def parse_args(argv=None):
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=50)
-    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--workload", default="square8192", choices=sorted(WORKLOADS))
     p.add_argument("--impl", default="ours", choices=["ours", "reference", "cublaslt"],
                    help="ours: this library; reference: the reference arithmetic on the host CPU; "
@@ -168,21 +169,25 @@ def shard_shape(w, world: int, rank: int):
     return M, n1 - n0, K, n0
 
 
-def time_steps(torch, step, steps, flush, stream, dev, barrier):
+def time_steps(torch, step, steps, flush, stream, dev, barrier, per_step=None):
     """Device milliseconds for `steps` calls of `step` on `stream`.
 
-    Operands far larger than L2: back-to-back steps between one event pair.
-    Otherwise a 256 MB buffer is overwritten before every step (outside the
-    timed pair, per-step events) so no step starts with its operands in L2."""
+    Operands far larger than L2: back-to-back steps, an event between every
+    two (the total runs from the first event to the last).  Otherwise a
+    256 MB buffer is overwritten before every step (outside the timed pair,
+    per-step events) so no step starts with its operands in L2.  The
+    per-step times go into `per_step` when a list is given."""
     if not flush:
-        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
         barrier()
-        ev0.record(stream)
-        for _ in range(steps):
+        evs[0].record(stream)
+        for i in range(steps):
             step()
-        ev1.record(stream)
+            evs[i + 1].record(stream)
         barrier()
-        return ev0.elapsed_time(ev1)
+        if per_step is not None:
+            per_step.extend(evs[i].elapsed_time(evs[i + 1]) for i in range(steps))
+        return evs[0].elapsed_time(evs[-1])
     scratch = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
              for _ in range(steps)]
@@ -193,9 +198,11 @@ def time_steps(torch, step, steps, flush, stream, dev, barrier):
         step()
         e1.record(stream)
     barrier()
-    ms = sum(e0.elapsed_time(e1) for e0, e1 in pairs)
+    times = [e0.elapsed_time(e1) for e0, e1 in pairs]
+    if per_step is not None:
+        per_step.extend(times)
     del scratch
-    return ms
+    return sum(times)
 
 
 def time_epilogue(gemm, torch, A, B, C, args, flush, stream, dev, barrier, flops):
@@ -266,12 +273,15 @@ def roofline(w, M, N, K, ms_per_launch, peaks, peak_kind, traffic):
         peak = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
         return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "peak_kind": f"{peak_kind} hbm_gbs (copy)",
+                "frac_of_spec": achieved / SPEC_PEAKS["hbm_gbs"],
                 "traffic": traffic, "algorithmic_bytes": alg_bytes,
                 "tflops": flops / (ms_per_launch / 1e3) / 1e12}
     achieved = flops / (ms_per_launch / 1e3) / 1e12
     peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    sustained = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
     return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
             "frac": achieved / peak, "peak_kind": f"{peak_kind} bf16_tflops (burst)",
+            "frac_of_sustained": achieved / sustained, "frac_of_spec": achieved / SPEC_PEAKS["bf16_tflops"],
             "traffic": traffic, "algorithmic_bytes": alg_bytes}
 
 
@@ -298,6 +308,16 @@ def cpu_sample_operands(w, seed: int, rows: int):
     return A, B
 
 
+def cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 def cpu_baseline(w, seed: int, target_s: float):
     """Multithreaded fp32 CPU GEMM on a row sample of the workload."""
     from oracle import oracle
@@ -312,9 +332,11 @@ def cpu_baseline(w, seed: int, target_s: float):
         A, B = cpu_sample_operands(w, seed, rows)
     dt, used = time_cpu_gemm(A, B, rows)
     tflops = 2.0 * rows * N * K / dt / 1e12
+    full_s = 2.0 * w["M"] * N * K / (tflops * 1e12)
     return {"value": tflops, "unit": "TFLOPS", "cores": used, "kind": "port",
-            "sample": f"{rows} of {w['M']} rows of C (full N={N}, K={K}) in {dt:.2f} s, fp32 accumulate",
-            "seconds": dt, "ncpus": oracle.num_cpus()}
+            "sample": f"{rows} of {w['M']} rows of C (full N={N}, K={K}) in {dt:.2f} s, fp32 accumulate; "
+                      f"the whole workload at this rate (linear in M) would take {full_s:.1f} s",
+            "seconds": dt, "ncpus": oracle.num_cpus(), "cpu_model": cpu_model()}
 
 
 def run_reference(args, w):
@@ -349,8 +371,9 @@ def run_reference(args, w):
                                          "dist": w["dist"], "rows_per_step": rows},
         "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": used, "kind": "port",
                          "sample": f"{rows} of {w['M']} rows of C per step (full N, K), "
-                                   "C restatement of the reference arithmetic, fp32 accumulate",
-                         "ncpus": oracle.num_cpus()},
+                                   "C restatement of the reference arithmetic, fp32 accumulate; "
+                                   "the rate extrapolates linearly in M to the whole workload",
+                         "ncpus": oracle.num_cpus(), "cpu_model": cpu_model()},
         "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -421,7 +444,8 @@ def run_ours(args, w):
     operand_bytes = (M * K + Nl * K) * 2
     flush = operand_bytes < 2 * L2_BYTES
     with ClockSampler(local) as clocks:
-        ms = time_steps(torch, step, args.steps, flush, stream, dev, barrier)
+        step_ms = []
+        ms = time_steps(torch, step, args.steps, flush, stream, dev, barrier, step_ms)
     st, detail = gemm.last_device_status()
     if st != _lib.OK:
         raise RuntimeError(f"device status {st} {detail}")
@@ -531,6 +555,9 @@ def run_ours(args, w):
             "gpu_launches": 0 if library_arm else args.steps,
             "launch": launch_shape(gemm, M, Nl, K, info, library_arm),
             "roofline": roofline(w, M, Nl, K, ms / args.steps, peaks, peak_kind, traffic),
+            "per_launch_ms": {"mean": ms / args.steps, "median": statistics.median(step_ms),
+                              "best": min(step_ms), "worst": max(step_ms),
+                              "how": "CUDA events between consecutive launches (rank 0)"},
             "clocks": clocks.summary(),
         }
         result.update(extra)
