@@ -186,7 +186,7 @@ class Gemm:
         """How a call with this shape would run on this handle now."""
         out = (ctypes.c_int * 6)()
         _lib.check(self._lib.b200gemm_plan(self._h, M, N, K, out), "b200gemm_plan")
-        kind = {1: "tiled", 2: "small_m"}.get(out[0], "?")
+        kind = {1: "tiled", 2: "small_m", 3: "small_m_1cta"}.get(out[0], "?")
         return {"kernel": kind, "tile_width": out[1], "tiles": out[2], "clusters": out[3],
                 "tail_split": out[4], "small_m_split": out[5]}
 

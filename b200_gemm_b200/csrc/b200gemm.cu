@@ -14,6 +14,7 @@
 #include "b200gemm.h"
 #include "gemm_decode_sm100.cuh"
 #include "gemm_sm100.cuh"
+#include "gemm_smallm1_sm100.cuh"
 #include "schedule.cuh"
 
 namespace b200gemm {
@@ -188,13 +189,83 @@ int prepare_kernel(int sm_count) {
 
 // Small-M instances (K split over 1, 2 or 4 CTA pairs of one cluster).
 template <class Cfg>
-bool prepare_decode_kernel() {
+int prepare_decode_kernel(int sm_count) {
   if (cudaFuncSetAttribute(gemm_bf16_nt_decode_sm100<Cfg>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes) != cudaSuccess) {
     cudaGetLastError();
-    return false;
+    return 0;
   }
-  return true;
+  if (Cfg::kClusterSize > 8 &&
+      cudaFuncSetAttribute(gemm_bf16_nt_decode_sm100<Cfg>, cudaFuncAttributeNonPortableClusterSizeAllowed,
+                           1) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  // Clusters of 2S CTAs that fit on the device at once: fewer than
+  // sm_count / 2S, since a cluster must sit inside one GPC.
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = Cfg::kClusterSize;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(static_cast<unsigned>(sm_count / Cfg::kClusterSize * Cfg::kClusterSize), 1, 1);
+  cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, gemm_bf16_nt_decode_sm100<Cfg>, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return clusters;
+}
+
+// Same for the single-CTA small-M kernel (clusters of S CTAs).
+template <class Cfg>
+int prepare_smallm1_kernel(int sm_count) {
+  if (cudaFuncSetAttribute(gemm_bf16_nt_smallm1_sm100<Cfg>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = Cfg::kSplit;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(static_cast<unsigned>(sm_count / Cfg::kSplit * Cfg::kSplit), 1, 1);
+  cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, gemm_bf16_nt_smallm1_sm100<Cfg>, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return clusters;
+}
+
+template <class Cfg>
+cudaError_t launch_smallm1(cudaStream_t stream, const CUtensorMap& ma, const CUtensorMap& mb,
+                           const CUtensorMap& mc, const SmallMParams& p) {
+  const unsigned clusters = static_cast<unsigned>((p.N + 127) / 128);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = Cfg::kSplit;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(clusters * Cfg::kSplit, 1, 1);
+  cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemm_bf16_nt_smallm1_sm100<Cfg>, ma, mb, mc, p);
 }
 
 template <class Cfg>
@@ -313,6 +384,8 @@ struct b200gemm_handle {
   int max_clusters = 0;       // co-resident 2-CTA clusters (the smaller of the two instances)
   int clusters_w[kNumWidths] = {};  // co-resident clusters of each width's instance
   int clusters_epi[kNumWidths] = {};  // the same for the fused-epilogue instances
+  int decode_clusters[5] = {};        // [S]: co-resident clusters of the small-M pair kernel, split S
+  int smallm1_clusters[5] = {};       // [S]: the same for the single-CTA small-M kernel
   int tile_width = 0;         // 0 = choose per call, else one of kWidths
   int small_m = -1;           // small-M kernel: -1 or 1 = use it when eligible, 0 = never
   unsigned int* status_dev = nullptr;
@@ -375,14 +448,20 @@ extern "C" int b200gemm_create(b200gemm_t* out, int device) {
                               prepare_kernel<CfgE128>(sms)};
   for (int i = 0; i < kNumWidths; ++i)
     if (cw[i] <= 0 || ce[i] <= 0) return B200GEMM_ERR_CUDA;
-  if (!prepare_decode_kernel<DecodeCfg<1>>() || !prepare_decode_kernel<DecodeCfg<2>>() ||
-      !prepare_decode_kernel<DecodeCfg<4>>()) {
-    return B200GEMM_ERR_CUDA;
-  }
+  const int dc1 = prepare_decode_kernel<DecodeCfg<1>>(sms), dc2 = prepare_decode_kernel<DecodeCfg<2>>(sms),
+            dc4 = prepare_decode_kernel<DecodeCfg<4>>(sms);
+  if (dc1 <= 0 || dc2 <= 0 || dc4 <= 0) return B200GEMM_ERR_CUDA;
+  const int sc2 = prepare_smallm1_kernel<SmallMCfg<2>>(sms), sc4 = prepare_smallm1_kernel<SmallMCfg<4>>(sms);
+  if (sc2 <= 0 || sc4 <= 0) return B200GEMM_ERR_CUDA;
 
   auto* h = new b200gemm_handle();
   h->device = device;
   h->sm_count = prop.multiProcessorCount;
+  h->decode_clusters[1] = dc1;
+  h->decode_clusters[2] = dc2;
+  h->decode_clusters[4] = dc4;
+  h->smallm1_clusters[2] = sc2;
+  h->smallm1_clusters[4] = sc4;
   h->max_clusters = cw[0];
   for (int i = 0; i < kNumWidths; ++i) {
     h->clusters_w[i] = cw[i];
@@ -602,16 +681,72 @@ namespace {
 
 // K split for the small-M kernel, or 0 when the tiled kernel should run:
 // M <= 128, N % 8 == 0 (its C stores are whole 16-byte groups), and the
-// largest split in {4, 2, 1} whose clusters fit on the device in one wave
-// while every CTA pair keeps at least two K blocks.
-int decode_split(int M, int N, int K, int sm_count) {
+// largest S in {4, 2} whose N / 256 clusters of 2S CTAs are all co-resident
+// (decode_clusters[S], from the occupancy query: a cluster must fit in one
+// GPC, so fewer than sm_count / 2S fit, and a second wave would double the
+// time) while every CTA pair keeps at least two K blocks, else 1.
+int decode_split(const b200gemm_handle* h, int M, int N, int K) {
   if (M > 128 || (N % 8) != 0 || K < 2 * kBlockK) return 0;
   const int clusters = (N + 255) / 256;
   const int num_kb = (K + kBlockK - 1) / kBlockK;
   for (int s : {4, 2}) {
-    if (clusters * 2 * s <= sm_count && num_kb >= 2 * s) return s;
+    if (clusters <= h->decode_clusters[s] && num_kb >= 2 * s) return s;
   }
   return 1;
+}
+
+// Which small-M kernel a shape takes: kind 0 = none (tiled kernel), 2 = the
+// pair kernel (256 rows of B per CTA pair), 3 = the single-CTA kernel (128
+// rows of B per CTA); split = its K split.  The pair kernel keeps more of B
+// in flight per SM (16 of its 24 KB stages against 16 of 32), so the
+// single-CTA kernel is taken only where it puts at least 1.5x the CTAs to
+// work, i.e. where the pair kernel's clusters cannot all co-reside at a
+// useful split (narrow N: N = 4096 gets 128 CTAs instead of 64).
+struct SmallMPlan {
+  int kind;
+  int split;
+};
+
+SmallMPlan smallm_plan(const b200gemm_handle* h, int M, int N, int K) {
+  const int sp = decode_split(h, M, N, K);
+  if (sp == 0) return {0, 0};
+  const int ctas_pair = (N + 255) / 256 * 2 * sp;
+  const int clusters1 = (N + 127) / 128;
+  const int num_kb = (K + kBlockK - 1) / kBlockK;
+  for (int s : {4, 2}) {  // (without a K split it never has 1.5x the pair kernel's CTAs)
+    if (clusters1 <= h->smallm1_clusters[s] && num_kb >= 2 * s) {
+      const int ctas_single = clusters1 * s;
+      if (2 * ctas_single >= 3 * ctas_pair && ctas_single <= h->sm_count) return {3, s};
+      break;
+    }
+  }
+  return {2, sp};
+}
+
+int run_smallm1(b200gemm_t h, int split, int M, int N, int K, const void* A, const void* B, void* C,
+                int ldc, cudaStream_t stream, unsigned long long timeout_ns) {
+  const uint64_t k = static_cast<uint64_t>(K);
+  CUtensorMap ma, mb, mc;
+  const uint32_t slice_rows = static_cast<uint32_t>(128 / split);
+  if (!encode_2d(&ma, A, k, static_cast<uint64_t>(M), k * 2, kBlockK, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_2d(&mb, B, k, static_cast<uint64_t>(N), k * 2, kBlockK, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_2d(&mc, C, static_cast<uint64_t>(N), static_cast<uint64_t>(M),
+                 static_cast<uint64_t>(ldc) * 2, 32, slice_rows, CU_TENSOR_MAP_SWIZZLE_NONE)) {
+    return B200GEMM_ERR_CUDA;
+  }
+  SmallMParams p;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.num_kb = (K + kBlockK - 1) / kBlockK;
+  p.kb_per_split = (p.num_kb + split - 1) / split;
+  p.status = h->status_dev;
+  p.timeout_ns = timeout_ns;
+  cudaError_t e;
+  if (split == 4) e = launch_smallm1<SmallMCfg<4>>(stream, ma, mb, mc, p);
+  else if (split == 2) e = launch_smallm1<SmallMCfg<2>>(stream, ma, mb, mc, p);
+  else return B200GEMM_ERR_INVALID_ARG;  // smallm_plan picks split 2 or 4
+  return e == cudaSuccess ? B200GEMM_OK : B200GEMM_ERR_CUDA;
 }
 
 int run_decode(b200gemm_t h, int split, int M, int N, int K, const void* A, const void* B, void* C,
@@ -645,7 +780,7 @@ int run_decode(b200gemm_t h, int split, int M, int N, int K, const void* A, cons
 extern "C" int b200gemm_small_m_split(b200gemm_t h, int M, int N, int K) {
   if (h == nullptr || M <= 0 || N <= 0 || K < 0) return 0;
   std::lock_guard<std::mutex> lock(h->mu);
-  return h->small_m != 0 ? decode_split(M, N, K, h->sm_count) : 0;
+  return h->small_m != 0 ? smallm_plan(h, M, N, K).split : 0;
 }
 
 extern "C" int b200gemm_set_small_m(b200gemm_t h, int mode) {
@@ -773,14 +908,15 @@ int gemm_device(b200gemm_t h, int M, int N, int K, const void* A, const void* B,
   }
 
   // Small M: stream B with every SM (operands swapped, K split in-cluster).
-  int split = 0;
+  SmallMPlan sm{0, 0};
   unsigned long long decode_timeout;
   {
     std::lock_guard<std::mutex> lock(h->mu);
-    split = (allow_small_m && !fused && h->small_m != 0) ? decode_split(M, N, K, h->sm_count) : 0;
+    if (allow_small_m && !fused && h->small_m != 0) sm = smallm_plan(h, M, N, K);
     decode_timeout = h->timeout_ns;
   }
-  if (split > 0) return run_decode(h, split, M, N, K, A, B, C, ldc, stream, decode_timeout);
+  if (sm.kind == 2) return run_decode(h, sm.split, M, N, K, A, B, C, ldc, stream, decode_timeout);
+  if (sm.kind == 3) return run_smallm1(h, sm.split, M, N, K, A, B, C, ldc, stream, decode_timeout);
 
   CUtensorMap ma, mb, mc;
   const uint32_t* sched = nullptr;
@@ -889,13 +1025,13 @@ extern "C" int b200gemm_plan(b200gemm_t h, int M, int N, int K, int* plan) {
   if (h == nullptr || plan == nullptr || M <= 0 || N <= 0 || K <= 0) return B200GEMM_ERR_INVALID_ARG;
   std::lock_guard<std::mutex> lock(h->mu);
   for (int i = 0; i < 6; ++i) plan[i] = 0;
-  const int split = h->small_m != 0 ? decode_split(M, N, K, h->sm_count) : 0;
-  if (split > 0) {
-    plan[0] = 2;  // small-M kernel
-    plan[1] = 256;
-    plan[2] = (N + 255) / 256;
+  const SmallMPlan sm = h->small_m != 0 ? smallm_plan(h, M, N, K) : SmallMPlan{0, 0};
+  if (sm.kind != 0) {
+    plan[0] = sm.kind;  // 2: small-M pair kernel, 3: small-M single-CTA kernel
+    plan[1] = sm.kind == 2 ? 256 : 128;  // rows of B per cluster
+    plan[2] = (N + plan[1] - 1) / plan[1];
     plan[3] = plan[2];
-    plan[5] = split;
+    plan[5] = sm.split;
     return B200GEMM_OK;
   }
   const int width = choose_tile_width(h, M, N, K);

@@ -180,8 +180,10 @@ int b200gemm_set_tile_width(b200gemm_t handle, int width);
 int b200gemm_set_tail_split(b200gemm_t handle, int enable);
 
 /* Launch plan a call with this shape would use now, in plan[0..5]: kernel
- * (1 tiled, 2 small-M), tile width, tiles, clusters launched, K split of the
- * last partial wave (1 = none; tiled kernel), K split of the small-M kernel. */
+ * (1 tiled, 2 small-M with 256 rows of B per CTA pair, 3 small-M with 128
+ * rows of B per CTA), tile width (tiled) or rows of B per cluster (small-M),
+ * tiles, clusters launched, K split of the last partial wave (1 = none;
+ * tiled kernel), K split of the small-M kernel. */
 int b200gemm_plan(b200gemm_t handle, int M, int N, int K, int* plan);
 
 /* The tile width (512, 256, 224, 192 or 128) a call with this shape would
@@ -195,8 +197,9 @@ int b200gemm_tile_width_for(b200gemm_t handle, int M, int N, int K);
  * 0: always use the tiled kernel.  The reference has no small-M path. */
 int b200gemm_set_small_m(b200gemm_t handle, int mode);
 
-/* The K split (1, 2 or 4) the small-M kernel would use for this shape on
- * this handle, or 0 when the tiled kernel would run. */
+/* The K split (1, 2 or 4) the small-M kernel (pair or single-CTA form, see
+ * b200gemm_plan) would use for this shape on this handle, or 0 when the
+ * tiled kernel would run. */
 int b200gemm_small_m_split(b200gemm_t handle, int M, int N, int K);
 
 /* Tile orders for the persistent schedule. */

@@ -1,6 +1,6 @@
-"""Parity of the small-M (decode-shaped) kernel: rows of B on the MMA's M
-side, K split over 1, 2 or 4 CTA pairs of a cluster, partial sums reduced
-through distributed shared memory.  Compared with the fp64 oracle
+"""Parity of the small-M (decode-shaped) kernels: rows of B on the MMA's M
+side, K split over 1, 2 or 4 CTA pairs (pair kernel) or CTAs (single-CTA
+kernel) of a cluster, partial sums reduced through distributed shared memory.  Compared with the fp64 oracle
 (|err| <= 2^-7 (|ref| + 1)) and, bit for bit where the K split is 1, with the
 tiled kernel."""
 import numpy as np
@@ -21,21 +21,29 @@ def _bits(t):
     return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
 
 
-# (M, N, K, expected split)
+# (M, N, K, kernel, split) on a 148-SM B200.  Pair kernel: 256 rows of B per
+# CTA pair, clusters of 2S CTAs (33 clusters of 4 and 15 of 8 fit at once);
+# single-CTA kernel: 128 rows of B per CTA, clusters of S, taken where it
+# puts at least 1.5x the CTAs to work (narrow N).
 CASES = [
-    (128, 4096, 1024, 4),
-    (128, 8192, 512, 2),
-    (64, 16384, 256, 1),
-    (1, 512, 1024, 4),
-    (77, 2048, 1000, 4),    # ragged M and K
-    (128, 2048, 576, 4),    # 9 K blocks over 4 pairs: the last pair has none
-    (100, 1032, 384, 2),    # N not a multiple of 256: the last cluster is ragged
+    (128, 4096, 1024, "small_m_1cta", 4),
+    (1, 4096, 4096, "small_m_1cta", 4),
+    (77, 3976, 1000, "small_m_1cta", 4),  # ragged M, N (3976 = 31 x 128 + 8) and K
+    (64, 9216, 512, "small_m_1cta", 2),
+    (128, 8192, 512, "small_m", 2),
+    (64, 16384, 256, "small_m", 1),
+    (1, 512, 1024, "small_m", 4),
+    (77, 2048, 1000, "small_m", 4),     # ragged M and K
+    (128, 2048, 576, "small_m", 4),     # 9 K blocks over 4 pairs: the last pair has none
+    (100, 1032, 384, "small_m", 2),     # N not a multiple of 256: the last cluster is ragged
 ]
 
 
-@pytest.mark.parametrize("M,N,K,split", CASES)
-def test_small_m_parity(gpu_handle, oracle_mod, M, N, K, split):
+@pytest.mark.parametrize("M,N,K,kernel,split", CASES)
+def test_small_m_parity(gpu_handle, oracle_mod, M, N, K, kernel, split):
     h = gpu_handle
+    plan = h.plan(M, N, K)
+    assert (plan["kernel"], plan["small_m_split"]) == (kernel, split), plan
     assert h.small_m_split(M, N, K) == split
     A_bits, B_bits = data.host_operands(M, N, K, "normal", seed=M * 7 + N + K)
     A, B = _dev(A_bits), _dev(B_bits)
