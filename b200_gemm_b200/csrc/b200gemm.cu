@@ -707,6 +707,40 @@ struct SmallMPlan {
   int split;
 };
 
+// Device-side epilogue arguments of a call (identity when epi is null).
+EpiArgs epi_args(const b200gemm_epilogue* epi) {
+  EpiArgs e{};
+  e.flags = 0;
+  e.act = B200GEMM_ACT_NONE;
+  e.out_type = B200GEMM_OUT_BF16;
+  e.alpha = 1.0f;
+  e.beta = 0.0f;
+  e.out_scale = 1.0f;
+  if (epi != nullptr) {
+    e.flags = (epi->bias != nullptr ? kEpiBias : 0u) | (epi->residual != nullptr ? kEpiResidual : 0u);
+    e.act = epi->activation;
+    e.out_type = epi->out_type;
+    e.alpha = epi->alpha;
+    e.beta = epi->beta;
+    e.out_scale = epi->out_scale == 0.0f ? 1.0f : epi->out_scale;
+    e.bias = static_cast<const uint16_t*>(epi->bias);
+    e.residual = static_cast<const uint16_t*>(epi->residual);
+    e.ldr = epi->ldr;
+  }
+  return e;
+}
+
+// C of the small-M kernels: boxes of 32 columns x slice_rows rows in the
+// output type, no swizzle (the transposing staging buffer is row-major).
+bool encode_smallm_c(CUtensorMap* mc, void* C, int M, int N, int ldc, uint32_t slice_rows, int out_type) {
+  const bool f32 = out_type == B200GEMM_OUT_F32, u8 = out_type == B200GEMM_OUT_E4M3;
+  const uint64_t esize = f32 ? 4 : (u8 ? 1 : 2);
+  return encode_2d(mc, C, static_cast<uint64_t>(N), static_cast<uint64_t>(M), static_cast<uint64_t>(ldc) * esize,
+                   32, slice_rows, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                       : (u8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16));
+}
+
 SmallMPlan smallm_plan(const b200gemm_handle* h, int M, int N, int K) {
   const int sp = decode_split(h, M, N, K);
   if (sp == 0) return {0, 0};
@@ -724,17 +758,18 @@ SmallMPlan smallm_plan(const b200gemm_handle* h, int M, int N, int K) {
 }
 
 int run_smallm1(b200gemm_t h, int split, int M, int N, int K, const void* A, const void* B, void* C,
-                int ldc, cudaStream_t stream, unsigned long long timeout_ns) {
+                int ldc, cudaStream_t stream, unsigned long long timeout_ns, const b200gemm_epilogue* epi) {
   const uint64_t k = static_cast<uint64_t>(K);
   CUtensorMap ma, mb, mc;
   const uint32_t slice_rows = static_cast<uint32_t>(128 / split);
+  const EpiArgs ea = epi_args(epi);
   if (!encode_2d(&ma, A, k, static_cast<uint64_t>(M), k * 2, kBlockK, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !encode_2d(&mb, B, k, static_cast<uint64_t>(N), k * 2, kBlockK, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !encode_2d(&mc, C, static_cast<uint64_t>(N), static_cast<uint64_t>(M),
-                 static_cast<uint64_t>(ldc) * 2, 32, slice_rows, CU_TENSOR_MAP_SWIZZLE_NONE)) {
+      !encode_smallm_c(&mc, C, M, N, ldc, slice_rows, ea.out_type)) {
     return B200GEMM_ERR_CUDA;
   }
-  SmallMParams p;
+  SmallMParams p{};
+  p.epi = ea;
   p.M = M;
   p.N = N;
   p.K = K;
@@ -750,17 +785,18 @@ int run_smallm1(b200gemm_t h, int split, int M, int N, int K, const void* A, con
 }
 
 int run_decode(b200gemm_t h, int split, int M, int N, int K, const void* A, const void* B, void* C,
-               int ldc, cudaStream_t stream, unsigned long long timeout_ns) {
+               int ldc, cudaStream_t stream, unsigned long long timeout_ns, const b200gemm_epilogue* epi) {
   const uint64_t k = static_cast<uint64_t>(K);
   CUtensorMap ma, mb, mc;
   const uint32_t slice_rows = static_cast<uint32_t>(128 / split);
+  const EpiArgs ea = epi_args(epi);
   if (!encode_2d(&ma, A, k, static_cast<uint64_t>(M), k * 2, kBlockK, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !encode_2d(&mb, B, k, static_cast<uint64_t>(N), k * 2, kBlockK, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !encode_2d(&mc, C, static_cast<uint64_t>(N), static_cast<uint64_t>(M),
-                 static_cast<uint64_t>(ldc) * 2, 32, slice_rows, CU_TENSOR_MAP_SWIZZLE_NONE)) {
+      !encode_smallm_c(&mc, C, M, N, ldc, slice_rows, ea.out_type)) {
     return B200GEMM_ERR_CUDA;
   }
-  DecodeParams p;
+  DecodeParams p{};
+  p.epi = ea;
   p.M = M;
   p.N = N;
   p.K = K;
@@ -804,8 +840,7 @@ extern "C" int b200gemm_bf16_nt(b200gemm_t h, int M, int N, int K, const void* A
 extern "C" int b200gemm_bf16_nt_epilogue(b200gemm_t h, int M, int N, int K, const void* A,
                                          const void* B, void* C, int ldc,
                                          const b200gemm_epilogue* epi, void* stream_ptr) {
-  if (epi == nullptr) return gemm_device(h, M, N, K, A, B, C, ldc, stream_ptr, true);
-  return gemm_device(h, M, N, K, A, B, C, ldc, stream_ptr, /*allow_small_m=*/false, 0, nullptr, epi);
+  return gemm_device(h, M, N, K, A, B, C, ldc, stream_ptr, /*allow_small_m=*/true, 0, nullptr, epi);
 }
 
 extern "C" int b200gemm_bf16_nt_allgather(b200gemm_t h, int M, int N, int K, const void* A,
@@ -910,13 +945,15 @@ int gemm_device(b200gemm_t h, int M, int N, int K, const void* A, const void* B,
   // Small M: stream B with every SM (operands swapped, K split in-cluster).
   SmallMPlan sm{0, 0};
   unsigned long long decode_timeout;
+  // Their C stores clip N in 16-byte units: e4m3 output needs N % 16 == 0.
+  const bool smallm_ok = allow_small_m && npeers == 0 && (c_type != B200GEMM_OUT_E4M3 || (N % 16) == 0);
   {
     std::lock_guard<std::mutex> lock(h->mu);
-    if (allow_small_m && !fused && h->small_m != 0) sm = smallm_plan(h, M, N, K);
+    if (smallm_ok && h->small_m != 0) sm = smallm_plan(h, M, N, K);
     decode_timeout = h->timeout_ns;
   }
-  if (sm.kind == 2) return run_decode(h, sm.split, M, N, K, A, B, C, ldc, stream, decode_timeout);
-  if (sm.kind == 3) return run_smallm1(h, sm.split, M, N, K, A, B, C, ldc, stream, decode_timeout);
+  if (sm.kind == 2) return run_decode(h, sm.split, M, N, K, A, B, C, ldc, stream, decode_timeout, epi);
+  if (sm.kind == 3) return run_smallm1(h, sm.split, M, N, K, A, B, C, ldc, stream, decode_timeout, epi);
 
   CUtensorMap ma, mb, mc;
   const uint32_t* sched = nullptr;

@@ -34,6 +34,7 @@ struct DecodeParams {
   int kb_per_split;  // K blocks per CTA pair
   unsigned int* status;
   unsigned long long timeout_ns;
+  EpiArgs epi;       // fused epilogue (identity: no flags, act none, bf16, alpha 1)
 };
 
 template <int S>
@@ -50,7 +51,7 @@ struct DecodeCfg {
   static constexpr int kRowBytes = kSliceRows * 4;           // one B row's fp32 partial slice
   static constexpr int kRecvSlotBytes = 128 * kRowBytes;
   static constexpr int kRecvBytes = (S - 1) * kRecvSlotBytes;
-  static constexpr int kCWarpBytes = kSliceRows * 32 * 2;    // kSliceRows x 32 bf16 per warp
+  static constexpr int kCWarpBytes = kSliceRows * 32 * 4;    // kSliceRows x 32 outputs (up to fp32) per warp
   static constexpr int kBarBytes = 256;
   // The ring takes every byte left: its depth is what hides HBM latency.
   static constexpr int kStagesFit = (232448 - 1024 - kBarBytes - kRecvBytes) / kStageBytes;
@@ -202,6 +203,17 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     const uint32_t t_row = tmem_base + ((quarter * 32u) << 16);
     const bool have = nkb > 0;                      // a pair with no K blocks contributes zeros
     bool ok = true;
+    if (p.epi.flags & kEpiResidual) {
+      // The residual rows this warp adds at the end, into L2 while B streams
+      // (one 128-byte line per row covers the warp's 32 columns).
+      const int colw = n0 + static_cast<int>(half) * 128 + static_cast<int>(quarter) * 32;
+      if (colw < p.N) {
+        for (int rr = static_cast<int>(lane); rr < Cfg::kSliceRows; rr += 32) {
+          const int r = static_cast<int>(pair) * Cfg::kSliceRows + rr;
+          if (r < p.M) ptx::prefetch_l2(p.epi.residual + static_cast<long long>(r) * p.epi.ldr + colw);
+        }
+      }
+    }
     if (have) {
       const bool got = ptx::mbar_wait(tfull, 0, wd, kSiteEpilogue, 0);
       ok = __all_sync(0xFFFFFFFFu, got);
@@ -243,7 +255,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       ok = __all_sync(0xFFFFFFFFu, got);
     }
     if (ok) {
-      const uint32_t cw = sC + (warp - 2u) * Cfg::kCWarpBytes;  // [kSliceRows][32] bf16
+      const uint32_t cw = sC + (warp - 2u) * Cfg::kCWarpBytes;  // [kSliceRows][32] outputs
+      const int row0 = static_cast<int>(pair) * Cfg::kSliceRows;
+      const int col = n0 + static_cast<int>(half) * 128 + static_cast<int>(quarter) * 32;
+      const bool epi_on = p.epi.flags != 0u || p.epi.act != kActNone || p.epi.alpha != 1.0f;
 #pragma unroll 1
       for (int c = 0; c < Cfg::kSliceRows / 32; ++c) {
         uint32_t v[32];
@@ -272,18 +287,13 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             acc[4 * g + 3] += __uint_as_float(x3);
           }
         }
+        if (epi_on) smallm_epilogue(acc, row0 + c * 32, col + static_cast<int>(lane), p.epi, p.M, p.N);
         // Transpose through shared memory: thread `lane` owns column `lane`
         // of the warp's 32-column block of C; rows are the slice's A rows.
-#pragma unroll
-        for (int t = 0; t < 32; ++t) {
-          const uint16_t b = __bfloat16_as_ushort(__float2bfloat16_rn(acc[t]));
-          ptx::st_shared_u16(cw + static_cast<uint32_t>(c * 32 + t) * 64u + lane * 2u, b);
-        }
+        smallm_stage(acc, cw, c, lane, p.epi.out_type, p.epi.out_scale);
       }
       ptx::fence_proxy_async_smem();
       __syncwarp();
-      const int row0 = static_cast<int>(pair) * Cfg::kSliceRows;
-      const int col = n0 + static_cast<int>(half) * 128 + static_cast<int>(quarter) * 32;
       if (lane == 0 && row0 < p.M && col < p.N) {
         ptx::tma_store_2d(&map_c, cw, col, row0);
         ptx::bulk_commit_group();

@@ -28,6 +28,7 @@
 
 #include <cstdint>
 #include <cuda.h>
+#include <cuda_bf16.h>
 
 #include "ptx_sm100.cuh"
 
@@ -356,6 +357,104 @@ __device__ __forceinline__ void epi_load_residual(const GemmParams& p, int r, in
   } else {
 #pragma unroll
     for (int i = 0; i < 16; ++i) q[i] = 0u;
+  }
+}
+
+// Fused-epilogue arguments of the small-M kernels (the tiled kernel keeps
+// the same fields in GemmParams).
+struct EpiArgs {
+  uint32_t flags;             // kEpiBias | kEpiResidual
+  int act;                    // kAct*
+  int out_type;               // kOutBf16, kOutF32, kOutE4m3
+  float alpha, beta, out_scale;
+  const uint16_t* bias;       // bf16[N]
+  const uint16_t* residual;   // bf16, row pitch ldr elements
+  long long ldr;
+};
+
+// Small-M kernels: the thread owns C column `col`; acc[t] is C[row0 + t][col]
+// (t < 32).  Applies D = act(alpha * acc + bias[col]) + beta * R[row][col]
+// in place; columns at or past N and rows at or past M read no memory.  The
+// activation switch sits outside straight 32-element loops and the residual
+// loads are issued together: a switch per element spreads the executed
+// instructions over the whole inlined code and misses the instruction cache
+// at every element.
+__device__ __forceinline__ void smallm_epilogue(float (&acc)[32], int row0, int col, const EpiArgs& e,
+                                                int M, int N) {
+  const bool in_n = col < N;
+  const float b = ((e.flags & kEpiBias) && in_n) ? __uint_as_float(static_cast<uint32_t>(__ldg(e.bias + col)) << 16)
+                                                 : 0.0f;
+  float q[32];
+  const bool res = (e.flags & kEpiResidual) != 0u;
+  if (res) {
+#pragma unroll
+    for (int t = 0; t < 32; ++t)
+      q[t] = (in_n && row0 + t < M)
+                 ? __uint_as_float(static_cast<uint32_t>(__ldg(e.residual + static_cast<long long>(row0 + t) * e.ldr + col)) << 16)
+                 : 0.0f;
+  }
+#pragma unroll
+  for (int t = 0; t < 32; ++t) acc[t] = fmaf(e.alpha, acc[t], b);
+  const bool fast = e.out_type != kOutF32;
+  switch (e.act) {
+    case kActRelu:
+#pragma unroll
+      for (int t = 0; t < 32; ++t) acc[t] = fmaxf(acc[t], 0.0f);
+      break;
+    case kActGelu:
+#pragma unroll
+      for (int t = 0; t < 32; ++t) acc[t] = 0.5f * acc[t] * (1.0f + erff(acc[t] * 0.70710678118654752f));
+      break;
+    case kActGeluTanh:
+      if (fast) {
+#pragma unroll
+        for (int t = 0; t < 32; ++t) {
+          const float x = acc[t];
+          acc[t] = 0.5f * x * (1.0f + ptx::tanh_approx(0.79788456080286536f * fmaf(0.044715f * x, x * x, x)));
+        }
+      } else {
+#pragma unroll
+        for (int t = 0; t < 32; ++t) {
+          const float x = acc[t];
+          acc[t] = 0.5f * x * (1.0f + tanhf(0.79788456080286536f * (x + 0.044715f * x * x * x)));
+        }
+      }
+      break;
+    case kActSilu:
+      if (fast) {
+#pragma unroll
+        for (int t = 0; t < 32; ++t) acc[t] = acc[t] * ptx::rcp_approx(1.0f + __expf(-acc[t]));
+      } else {
+#pragma unroll
+        for (int t = 0; t < 32; ++t) acc[t] = acc[t] / (1.0f + expf(-acc[t]));
+      }
+      break;
+    default:
+      break;
+  }
+  if (res) {
+#pragma unroll
+    for (int t = 0; t < 32; ++t) acc[t] = fmaf(e.beta, q[t], acc[t]);
+  }
+}
+
+// Small-M kernels: one chunk of 32 rows of C for the warp's 32 columns into
+// the transposing staging buffer [rows][32 columns] in the output type
+// (bf16: 64-byte rows, fp32: 128, e4m3: 32); `lane` = the column.
+__device__ __forceinline__ void smallm_stage(const float (&acc)[32], uint32_t cw, int c, uint32_t lane,
+                                             int out_type, float out_scale) {
+#pragma unroll
+  for (int t = 0; t < 32; ++t) {
+    const uint32_t row = static_cast<uint32_t>(c * 32 + t);
+    if (out_type == kOutF32) {
+      asm volatile("st.shared.u32 [%0], %1;" ::"r"(cw + row * 128u + lane * 4u), "r"(__float_as_uint(acc[t]))
+                   : "memory");
+    } else if (out_type == kOutE4m3) {
+      const uint32_t q = ptx::pack_e4m3x4(out_scale * acc[t], 0.0f, 0.0f, 0.0f) & 0xFFu;
+      asm volatile("st.shared.u8 [%0], %1;" ::"r"(cw + row * 32u + lane), "r"(q) : "memory");
+    } else {
+      ptx::st_shared_u16(cw + row * 64u + lane * 2u, __bfloat16_as_ushort(__float2bfloat16_rn(acc[t])));
+    }
   }
 }
 

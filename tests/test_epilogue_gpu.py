@@ -93,10 +93,39 @@ def test_epilogue_terms_and_widths(gpu_handle, oracle_mod, use_bias, use_res, wi
         h.set_tile_width(0)
 
 
-@pytest.mark.parametrize("M", [1, 64, 128])
-def test_epilogue_small_m_runs_tiled(gpu_handle, oracle_mod, M):
-    """Small M takes the tiled kernel with the epilogue (the small-M kernel has none)."""
-    _case(gpu_handle, oracle_mod, M, 1024, 512, "silu", True, True, 1.0, 1.0, torch.bfloat16, seed=M)
+# (M, N, K, small-M kernel the plan picks)
+SMALL_M = [(1, 1024, 512, "small_m"), (64, 4096, 1024, "small_m_1cta"), (128, 8192, 512, "small_m"),
+           (77, 1040, 384, "small_m"), (100, 3968, 704, "small_m_1cta")]
+
+
+@pytest.mark.parametrize("M,N,K,kernel", SMALL_M)
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32], ids=["bf16", "f32"])
+def test_epilogue_small_m(gpu_handle, oracle_mod, M, N, K, kernel, out_dtype):
+    """Small M keeps the small-M kernels (pair or single-CTA) with the epilogue."""
+    assert gpu_handle.plan(M, N, K)["kernel"] == kernel
+    for act, use_bias, use_res in (("silu", True, True), ("gelu", True, False), ("none", False, True)):
+        _case(gpu_handle, oracle_mod, M, N, K, act, use_bias, use_res, 0.5, -1.0, out_dtype, seed=M + N)
+
+
+@pytest.mark.parametrize("M,N,K,kernel", SMALL_M)
+def test_epilogue_small_m_e4m3(gpu_handle, oracle_mod, M, N, K, kernel):
+    if N % 16:
+        pytest.skip("e4m3 small-M output needs N % 16 == 0 (the tiled kernel covers the rest)")
+    _e4m3_case(gpu_handle, oracle_mod, M, N, K, "gelu_tanh", True, True, 8.0, seed=M + 2 * N)
+
+
+@pytest.mark.parametrize("M,N,K,kernel", SMALL_M)
+def test_small_m_identity_epilogue_bit_exact(gpu_handle, M, N, K, kernel):
+    """No terms: the same small-M kernel writes what the plain call writes;
+    fp32 output rounded to bf16 is the plain call's output too."""
+    h = gpu_handle
+    A, B = data.device_operands(M, N, K, "normal", seed=3)
+    C0 = h.bf16_nt(A, B)
+    C1 = h.bf16_nt_epilogue(A, B)
+    C2 = h.bf16_nt_epilogue(A, B, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert torch.equal(C0.view(torch.int16), C1.view(torch.int16))
+    assert torch.equal(C0.view(torch.int16), C2.to(torch.bfloat16).view(torch.int16))
 
 
 def test_large_activation_range(gpu_handle, oracle_mod):
