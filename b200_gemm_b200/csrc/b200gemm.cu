@@ -251,7 +251,7 @@ int prepare_smallm1_kernel(int sm_count) {
 
 template <class Cfg>
 cudaError_t launch_smallm1(cudaStream_t stream, const CUtensorMap& ma, const CUtensorMap& mb,
-                           const CUtensorMap& mc, const SmallMParams& p) {
+                           const CUtensorMap& mc, const CUtensorMap& mr, const SmallMParams& p) {
   const unsigned clusters = static_cast<unsigned>((p.N + 127) / 128);
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
@@ -265,12 +265,12 @@ cudaError_t launch_smallm1(cudaStream_t stream, const CUtensorMap& ma, const CUt
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemm_bf16_nt_smallm1_sm100<Cfg>, ma, mb, mc, p);
+  return cudaLaunchKernelEx(&cfg, gemm_bf16_nt_smallm1_sm100<Cfg>, ma, mb, mc, mr, p);
 }
 
 template <class Cfg>
 cudaError_t launch_decode(cudaStream_t stream, const CUtensorMap& ma, const CUtensorMap& mb,
-                          const CUtensorMap& mc, const DecodeParams& p) {
+                          const CUtensorMap& mc, const CUtensorMap& mr, const DecodeParams& p) {
   const unsigned clusters = static_cast<unsigned>((p.N + 255) / 256);
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
@@ -284,7 +284,7 @@ cudaError_t launch_decode(cudaStream_t stream, const CUtensorMap& ma, const CUte
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemm_bf16_nt_decode_sm100<Cfg>, ma, mb, mc, p);
+  return cudaLaunchKernelEx(&cfg, gemm_bf16_nt_decode_sm100<Cfg>, ma, mb, mc, mr, p);
 }
 
 template <class Cfg>
@@ -732,6 +732,19 @@ EpiArgs epi_args(const b200gemm_epilogue* epi) {
 
 // C of the small-M kernels: boxes of 32 columns x slice_rows rows in the
 // output type, no swizzle (the transposing staging buffer is row-major).
+// The residual of a fused epilogue for the small-M kernels: the same boxes
+// (32 columns x slice_rows rows) of the bf16 M x N matrix with pitch ldr;
+// without a residual the C map stands in (the kernels then never read it).
+bool encode_smallm_r(CUtensorMap* mr, const CUtensorMap& mc, const b200gemm_epilogue* epi, int M, int N,
+                     uint32_t slice_rows) {
+  if (epi == nullptr || epi->residual == nullptr) {
+    *mr = mc;
+    return true;
+  }
+  return encode_2d(mr, epi->residual, static_cast<uint64_t>(N), static_cast<uint64_t>(M),
+                   static_cast<uint64_t>(epi->ldr) * 2, 32, slice_rows, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
 bool encode_smallm_c(CUtensorMap* mc, void* C, int M, int N, int ldc, uint32_t slice_rows, int out_type) {
   const bool f32 = out_type == B200GEMM_OUT_F32, u8 = out_type == B200GEMM_OUT_E4M3;
   const uint64_t esize = f32 ? 4 : (u8 ? 1 : 2);
@@ -760,12 +773,13 @@ SmallMPlan smallm_plan(const b200gemm_handle* h, int M, int N, int K) {
 int run_smallm1(b200gemm_t h, int split, int M, int N, int K, const void* A, const void* B, void* C,
                 int ldc, cudaStream_t stream, unsigned long long timeout_ns, const b200gemm_epilogue* epi) {
   const uint64_t k = static_cast<uint64_t>(K);
-  CUtensorMap ma, mb, mc;
+  CUtensorMap ma, mb, mc, mr;
   const uint32_t slice_rows = static_cast<uint32_t>(128 / split);
   const EpiArgs ea = epi_args(epi);
   if (!encode_2d(&ma, A, k, static_cast<uint64_t>(M), k * 2, kBlockK, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !encode_2d(&mb, B, k, static_cast<uint64_t>(N), k * 2, kBlockK, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !encode_smallm_c(&mc, C, M, N, ldc, slice_rows, ea.out_type)) {
+      !encode_smallm_c(&mc, C, M, N, ldc, slice_rows, ea.out_type) ||
+      !encode_smallm_r(&mr, mc, epi, M, N, slice_rows)) {
     return B200GEMM_ERR_CUDA;
   }
   SmallMParams p{};
@@ -778,8 +792,8 @@ int run_smallm1(b200gemm_t h, int split, int M, int N, int K, const void* A, con
   p.status = h->status_dev;
   p.timeout_ns = timeout_ns;
   cudaError_t e;
-  if (split == 4) e = launch_smallm1<SmallMCfg<4>>(stream, ma, mb, mc, p);
-  else if (split == 2) e = launch_smallm1<SmallMCfg<2>>(stream, ma, mb, mc, p);
+  if (split == 4) e = launch_smallm1<SmallMCfg<4>>(stream, ma, mb, mc, mr, p);
+  else if (split == 2) e = launch_smallm1<SmallMCfg<2>>(stream, ma, mb, mc, mr, p);
   else return B200GEMM_ERR_INVALID_ARG;  // smallm_plan picks split 2 or 4
   return e == cudaSuccess ? B200GEMM_OK : B200GEMM_ERR_CUDA;
 }
@@ -787,12 +801,13 @@ int run_smallm1(b200gemm_t h, int split, int M, int N, int K, const void* A, con
 int run_decode(b200gemm_t h, int split, int M, int N, int K, const void* A, const void* B, void* C,
                int ldc, cudaStream_t stream, unsigned long long timeout_ns, const b200gemm_epilogue* epi) {
   const uint64_t k = static_cast<uint64_t>(K);
-  CUtensorMap ma, mb, mc;
+  CUtensorMap ma, mb, mc, mr;
   const uint32_t slice_rows = static_cast<uint32_t>(128 / split);
   const EpiArgs ea = epi_args(epi);
   if (!encode_2d(&ma, A, k, static_cast<uint64_t>(M), k * 2, kBlockK, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !encode_2d(&mb, B, k, static_cast<uint64_t>(N), k * 2, kBlockK, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !encode_smallm_c(&mc, C, M, N, ldc, slice_rows, ea.out_type)) {
+      !encode_smallm_c(&mc, C, M, N, ldc, slice_rows, ea.out_type) ||
+      !encode_smallm_r(&mr, mc, epi, M, N, slice_rows)) {
     return B200GEMM_ERR_CUDA;
   }
   DecodeParams p{};
@@ -805,9 +820,9 @@ int run_decode(b200gemm_t h, int split, int M, int N, int K, const void* A, cons
   p.status = h->status_dev;
   p.timeout_ns = timeout_ns;
   cudaError_t e;
-  if (split == 4) e = launch_decode<DecodeCfg<4>>(stream, ma, mb, mc, p);
-  else if (split == 2) e = launch_decode<DecodeCfg<2>>(stream, ma, mb, mc, p);
-  else e = launch_decode<DecodeCfg<1>>(stream, ma, mb, mc, p);
+  if (split == 4) e = launch_decode<DecodeCfg<4>>(stream, ma, mb, mc, mr, p);
+  else if (split == 2) e = launch_decode<DecodeCfg<2>>(stream, ma, mb, mc, mr, p);
+  else e = launch_decode<DecodeCfg<1>>(stream, ma, mb, mc, mr, p);
   return e == cudaSuccess ? B200GEMM_OK : B200GEMM_ERR_CUDA;
 }
 

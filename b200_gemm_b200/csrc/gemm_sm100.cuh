@@ -374,25 +374,17 @@ struct EpiArgs {
 
 // Small-M kernels: the thread owns C column `col`; acc[t] is C[row0 + t][col]
 // (t < 32).  Applies D = act(alpha * acc + bias[col]) + beta * R[row][col]
-// in place; columns at or past N and rows at or past M read no memory.  The
-// activation switch sits outside straight 32-element loops and the residual
-// loads are issued together: a switch per element spreads the executed
-// instructions over the whole inlined code and misses the instruction cache
-// at every element.
-__device__ __forceinline__ void smallm_epilogue(float (&acc)[32], int row0, int col, const EpiArgs& e,
-                                                int M, int N) {
+// in place.  R comes from the warp's residual tile in shared memory (loaded
+// by TMA, zeros outside M and N): element t of this thread at
+// rtile + 64 t.  The activation switch sits outside straight 32-element
+// loops: a switch per element spreads the executed instructions over the
+// whole inlined code and misses the instruction cache at every element.
+__device__ __forceinline__ void smallm_epilogue(float (&acc)[32], int col, const EpiArgs& e, int N,
+                                                uint32_t rtile) {
   const bool in_n = col < N;
   const float b = ((e.flags & kEpiBias) && in_n) ? __uint_as_float(static_cast<uint32_t>(__ldg(e.bias + col)) << 16)
                                                  : 0.0f;
-  float q[32];
   const bool res = (e.flags & kEpiResidual) != 0u;
-  if (res) {
-#pragma unroll
-    for (int t = 0; t < 32; ++t)
-      q[t] = (in_n && row0 + t < M)
-                 ? __uint_as_float(static_cast<uint32_t>(__ldg(e.residual + static_cast<long long>(row0 + t) * e.ldr + col)) << 16)
-                 : 0.0f;
-  }
 #pragma unroll
   for (int t = 0; t < 32; ++t) acc[t] = fmaf(e.alpha, acc[t], b);
   const bool fast = e.out_type != kOutF32;
@@ -434,7 +426,11 @@ __device__ __forceinline__ void smallm_epilogue(float (&acc)[32], int row0, int 
   }
   if (res) {
 #pragma unroll
-    for (int t = 0; t < 32; ++t) acc[t] = fmaf(e.beta, q[t], acc[t]);
+    for (int t = 0; t < 32; ++t) {
+      uint16_t r;
+      asm volatile("ld.shared.u16 %0, [%1];" : "=h"(r) : "r"(rtile + static_cast<uint32_t>(t) * 64u) : "memory");
+      acc[t] = fmaf(e.beta, __uint_as_float(static_cast<uint32_t>(r) << 16), acc[t]);
+    }
   }
 }
 

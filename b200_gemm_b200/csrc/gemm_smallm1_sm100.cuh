@@ -53,18 +53,20 @@ struct SmallMCfg {
   static constexpr int kRecvSlotBytes = kRowsB * kRowBytes;
   static constexpr int kRecvBytes = (S - 1) * kRecvSlotBytes;
   static constexpr int kCWarpBytes = kSliceRows * 32 * 4;    // kSliceRows x 32 outputs (up to fp32) per warp
+  static constexpr int kRWarpBytes = kSliceRows * 32 * 2;    // the same rows of the residual (bf16)
   static constexpr int kBarBytes = 256;
   static constexpr int kStagesFit = (232448 - 1024 - kBarBytes - kRecvBytes) / kStageBytes;
   static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
   static_assert(kStages >= 4, "pipeline too shallow");
-  static_assert(4 * kCWarpBytes <= kStages * kStageB, "C staging aliases the B stages");
+  static_assert(4 * (kCWarpBytes + kRWarpBytes) <= kStages * kStageB, "C staging and residual tiles alias the B stages");
   static constexpr int kB = 0;       // B stages; after the last MMA they hold the C staging buffers
   static constexpr int kA = kB + kStages * kStageB;
   static constexpr int kRecv = kA + kStages * kStageA;
   static constexpr int kFull = kRecv + kRecvBytes;
   static constexpr int kEmpty = kFull + 8 * kStages;
   static constexpr int kTFull = kEmpty + 8 * kStages;
-  static constexpr int kRecvBar = kTFull + 8;
+  static constexpr int kResBar = kTFull + 8;   // one per epilogue warp: its residual tile landed
+  static constexpr int kRecvBar = kResBar + 32;
   static constexpr int kDrain = kRecvBar + 8;
   static constexpr int kTmemSlot = kDrain + 8;
   static constexpr int kAbort = kTmemSlot + 4;
@@ -83,7 +85,8 @@ template <class Cfg>
 __global__ void __launch_bounds__(Cfg::kThreads, 1)
     gemm_bf16_nt_smallm1_sm100(const __grid_constant__ CUtensorMap map_a,
                                const __grid_constant__ CUtensorMap map_b,
-                               const __grid_constant__ CUtensorMap map_c, const SmallMParams p) {
+                               const __grid_constant__ CUtensorMap map_c,
+                               const __grid_constant__ CUtensorMap map_r, const SmallMParams p) {
   constexpr int S = Cfg::kSplit;
   constexpr int STAGES = Cfg::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -118,6 +121,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       ptx::mbar_init(empty0 + 8 * s, 1);
     }
     ptx::mbar_init(tfull, 1);
+    for (int w = 0; w < 4; ++w) ptx::mbar_init(base + Cfg::kResBar + 8 * w, 1);
     ptx::mbar_init(recv_bar, 1);
     ptx::mbar_init(drain, 1);
     ptx::fence_mbar_init_cluster();
@@ -127,6 +131,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     ptx::prefetch_tensormap(&map_a);
     ptx::prefetch_tensormap(&map_b);
     ptx::prefetch_tensormap(&map_c);
+    if (p.epi.flags & kEpiResidual) ptx::prefetch_tensormap(&map_r);
   }
   if (warp == 1) {
     ptx::tmem_alloc_cg1(tmem_slot, Cfg::kNT);
@@ -195,21 +200,22 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     const uint32_t t_row = tmem_base + ((quarter * 32u) << 16);
     const bool have = nkb > 0;                      // a CTA with no K blocks contributes zeros
     bool ok = true;
-    if (p.epi.flags & kEpiResidual) {
-      // The residual rows this warp adds at the end, into L2 while B streams
-      // (one 128-byte line per row covers the warp's 32 columns).
-      const int colw = n0 + static_cast<int>(quarter) * 32;
-      if (colw < p.N) {
-        for (int rr = static_cast<int>(lane); rr < Cfg::kSliceRows; rr += 32) {
-          const int r = static_cast<int>(rank) * Cfg::kSliceRows + rr;
-          if (r < p.M) ptx::prefetch_l2(p.epi.residual + static_cast<long long>(r) * p.epi.ldr + colw);
-        }
-      }
-    }
     if (have) {
       const bool got = ptx::mbar_wait(tfull, 0, wd, kSiteEpilogue, 0);
       ok = __all_sync(0xFFFFFFFFu, got);
       ptx::tc_fence_after();
+    }
+    // The residual rows and columns this warp adds at the end: one TMA load
+    // into the B stages (free once the MMAs are done), in flight during the
+    // exchange below.  Rows past M and columns past N read as zeros.
+    const int row0 = static_cast<int>(rank) * Cfg::kSliceRows;
+    const int col = n0 + static_cast<int>(quarter) * 32;
+    const uint32_t res_bar = base + Cfg::kResBar + 8 * (warp - 2u);
+    const uint32_t rtile = sC + 4 * Cfg::kCWarpBytes + (warp - 2u) * Cfg::kRWarpBytes;
+    const bool res_load = ok && (p.epi.flags & kEpiResidual) && row0 < p.M && col < p.N;
+    if (res_load && lane == 0) {
+      ptx::mbar_arrive_expect_tx(res_bar, Cfg::kRWarpBytes);
+      ptx::tma_load_2d(rtile, &map_r, res_bar, col, row0, ptx::policy_evict_first());
     }
     // 1. Send the slices that the other CTAs finish.
     if (ok && S > 1) {
@@ -247,9 +253,11 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     }
     if (ok) {
       const uint32_t cw = sC + (warp - 2u) * Cfg::kCWarpBytes;  // [kSliceRows][32] outputs
-      const int row0 = static_cast<int>(rank) * Cfg::kSliceRows;
-      const int col = n0 + static_cast<int>(quarter) * 32;
       const bool epi_on = p.epi.flags != 0u || p.epi.act != kActNone || p.epi.alpha != 1.0f;
+      if (res_load) {
+        const bool got = ptx::mbar_wait(res_bar, 0, wd, kSiteEpilogue, 2);
+        ok = __all_sync(0xFFFFFFFFu, got);
+      }
 #pragma unroll 1
       for (int c = 0; c < Cfg::kSliceRows / 32; ++c) {
         uint32_t v[32];
@@ -278,7 +286,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             acc[4 * g + 3] += __uint_as_float(x3);
           }
         }
-        if (epi_on) smallm_epilogue(acc, row0 + c * 32, col + static_cast<int>(lane), p.epi, p.M, p.N);
+        if (epi_on) smallm_epilogue(acc, col + static_cast<int>(lane), p.epi, p.N, rtile + c * 32 * 64 + lane * 2);
         // Transpose through shared memory: thread `lane` owns column `lane`
         // of the warp's 32-column block of C; rows are the slice's A rows.
         smallm_stage(acc, cw, c, lane, p.epi.out_type, p.epi.out_scale);
