@@ -254,10 +254,14 @@ def launch_shape(gemm, M, N, K, info, library_arm):
     if library_arm:
         return None
     plan = gemm.plan(M, N, K)
-    if plan["kernel"] == "small_m":
+    if plan["kernel"] == "small_m":  # CTA pairs of 256 rows of B, clusters of 2 x split
         split = plan["small_m_split"]
         return dict(info, kernel="small_m", ctas=plan["tiles"] * 2 * split, threads_per_cta=192,
                     cluster=2 * split)
+    if plan["kernel"] == "small_m_1cta":  # CTAs of 128 rows of B, clusters of split
+        split = plan["small_m_split"]
+        return dict(info, kernel="small_m_1cta", ctas=plan["tiles"] * split, threads_per_cta=192,
+                    cluster=split)
     return dict(info, kernel="tiled", clusters=plan["clusters"], tiles=plan["tiles"],
                 threads_per_cta=576 if plan["tile_width"] == 512 else 192, cluster=2)
 
@@ -568,7 +572,7 @@ def run_ours(args, w):
             plan = gemm.plan(M, Nl, K)
             result["kernel"] = plan["kernel"]
             result["tile_width"] = plan["tile_width"] if plan["kernel"] == "tiled" else None
-            if plan["kernel"] == "small_m":
+            if plan["kernel"].startswith("small_m"):
                 result["small_m_split"] = plan["small_m_split"]
         if not args.no_cpu_baseline and not library_arm:
             result["cpu_baseline"] = cpu_baseline(w, args.seed, args.cpu_seconds)
