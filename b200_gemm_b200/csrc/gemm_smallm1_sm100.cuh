@@ -137,19 +137,33 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     ptx::tmem_alloc_cg1(tmem_slot, Cfg::kNT);
     ptx::tmem_relinquish_cg1();
   }
+  // The producer's loads signal only this CTA's barriers (initialised above
+  // by this same thread), so the first ring of them goes out between the
+  // two halves of the cluster barrier instead of after the whole prologue.
+  const uint64_t policy_b = ptx::policy_evict_first();  // B is read once
+  const uint64_t policy_a = ptx::policy_evict_last();   // A is read by every cluster
+  const int early = nkb < STAGES ? nkb : STAGES;
   ptx::tc_fence_before();
-  ptx::cluster_sync_all();
+  ptx::cluster_arrive();
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < early; ++s) {
+      const int kb = kb_begin + s;
+      ptx::mbar_arrive_expect_tx(full0 + 8 * s, Cfg::kStageBytes);
+      ptx::tma_load_2d(sB + s * Cfg::kStageB, &map_b, full0 + 8 * s, kb * kBlockK, n0, policy_b);
+      ptx::tma_load_2d(sA + s * Cfg::kStageA, &map_a, full0 + 8 * s, kb * kBlockK, 0, policy_a);
+    }
+  }
+  ptx::cluster_wait();
   ptx::tc_fence_after();
   uint32_t tmem_base;
   asm volatile("ld.shared.u32 %0, [%1];" : "=r"(tmem_base) : "r"(tmem_slot) : "memory");
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0 && nkb > 0) {
-      const uint64_t policy_b = ptx::policy_evict_first();  // B is read once
-      const uint64_t policy_a = ptx::policy_evict_last();   // A is read by every cluster
-      uint32_t stage = 0, phase = 0;
-      for (int kb = kb_begin; kb < kb_end; ++kb) {
+    if (lane == 0 && nkb > early) {
+      uint32_t stage = early == STAGES ? 0u : static_cast<uint32_t>(early);
+      uint32_t phase = early == STAGES ? 1u : 0u;
+      for (int kb = kb_begin + early; kb < kb_end; ++kb) {
         if (!ptx::mbar_wait(empty0 + 8 * stage, phase ^ 1u, wd, kSiteProducer, 0)) break;
         ptx::mbar_arrive_expect_tx(full0 + 8 * stage, Cfg::kStageBytes);
         ptx::tma_load_2d(sB + stage * Cfg::kStageB, &map_b, full0 + 8 * stage, kb * kBlockK, n0, policy_b);
