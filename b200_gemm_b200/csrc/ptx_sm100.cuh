@@ -383,10 +383,6 @@ __device__ __forceinline__ void reg_fence32(uint32_t* r) {
                  "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]),
                  "+r"(r[30]), "+r"(r[31]));
 }
-__device__ __forceinline__ void reg_fence64(uint32_t (&r)[64]) {
-  reg_fence32(&r[0]);
-  reg_fence32(&r[32]);
-}
 
 // Two fp32 -> packed bf16x2 with round-to-nearest-even (lo in bits 0-15).
 __device__ __forceinline__ uint32_t pack_bf16x2(uint32_t lo_f32, uint32_t hi_f32) {
