@@ -331,15 +331,20 @@ def cpu_baseline(w, seed: int, target_s: float):
     A, B = cpu_sample_operands(w, seed, max(probe_rows, 256))
     dt, used = time_cpu_gemm(A, B, probe_rows)
     rate = 2.0 * probe_rows * N * K / max(dt, 1e-9)
-    rows = min(A.shape[0], cpu_rows_for(target_s, N, K, used, rate))
+    rows = cpu_rows_for(target_s, N, K, used, rate)
+    if rows * 2 >= w["M"]:
+        rows = w["M"]  # within twice the target: run the whole workload, no extrapolation
+    rows = min(rows, w["M"])
     if rows > A.shape[0]:
         A, B = cpu_sample_operands(w, seed, rows)
     dt, used = time_cpu_gemm(A, B, rows)
     tflops = 2.0 * rows * N * K / dt / 1e12
     full_s = 2.0 * w["M"] * N * K / (tflops * 1e12)
+    sample = (f"the whole workload ({w['M']} x {N} x {K}) in {dt:.2f} s, fp32 accumulate" if rows == w["M"] else
+              f"{rows} of {w['M']} rows of C (full N={N}, K={K}) in {dt:.2f} s, fp32 accumulate; "
+              f"the whole workload at this rate (linear in M) would take {full_s:.1f} s")
     return {"value": tflops, "unit": "TFLOPS", "cores": used, "kind": "port",
-            "sample": f"{rows} of {w['M']} rows of C (full N={N}, K={K}) in {dt:.2f} s, fp32 accumulate; "
-                      f"the whole workload at this rate (linear in M) would take {full_s:.1f} s",
+            "sample": sample,
             "seconds": dt, "ncpus": oracle.num_cpus(), "cpu_model": cpu_model()}
 
 
