@@ -439,18 +439,23 @@ __device__ __forceinline__ void smallm_epilogue(float (&acc)[32], int col, const
 // (bf16: 64-byte rows, fp32: 128, e4m3: 32); `lane` = the column.
 __device__ __forceinline__ void smallm_stage(const float (&acc)[32], uint32_t cw, int c, uint32_t lane,
                                              int out_type, float out_scale) {
+  // One branch per chunk, straight loops inside (see smallm_epilogue).
+  const uint32_t row0 = static_cast<uint32_t>(c * 32);
+  if (out_type == kOutF32) {
 #pragma unroll
-  for (int t = 0; t < 32; ++t) {
-    const uint32_t row = static_cast<uint32_t>(c * 32 + t);
-    if (out_type == kOutF32) {
-      asm volatile("st.shared.u32 [%0], %1;" ::"r"(cw + row * 128u + lane * 4u), "r"(__float_as_uint(acc[t]))
+    for (int t = 0; t < 32; ++t)
+      asm volatile("st.shared.u32 [%0], %1;" ::"r"(cw + (row0 + t) * 128u + lane * 4u), "r"(__float_as_uint(acc[t]))
                    : "memory");
-    } else if (out_type == kOutE4m3) {
+  } else if (out_type == kOutE4m3) {
+#pragma unroll
+    for (int t = 0; t < 32; ++t) {
       const uint32_t q = ptx::pack_e4m3x4(out_scale * acc[t], 0.0f, 0.0f, 0.0f) & 0xFFu;
-      asm volatile("st.shared.u8 [%0], %1;" ::"r"(cw + row * 32u + lane), "r"(q) : "memory");
-    } else {
-      ptx::st_shared_u16(cw + row * 64u + lane * 2u, __bfloat16_as_ushort(__float2bfloat16_rn(acc[t])));
+      asm volatile("st.shared.u8 [%0], %1;" ::"r"(cw + (row0 + t) * 32u + lane), "r"(q) : "memory");
     }
+  } else {
+#pragma unroll
+    for (int t = 0; t < 32; ++t)
+      ptx::st_shared_u16(cw + (row0 + t) * 64u + lane * 2u, __bfloat16_as_ushort(__float2bfloat16_rn(acc[t])));
   }
 }
 

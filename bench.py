@@ -327,7 +327,9 @@ def cpu_baseline(w, seed: int, target_s: float):
     from oracle import oracle
 
     N, K = w["N"], w["K"]
-    probe_rows = 4
+    # Calibrate on enough rows to occupy every thread (a few rows measure
+    # thread start-up, not the GEMM), then size the sample from that rate.
+    probe_rows = min(w["M"], 8 * max(1, os.cpu_count() or 1))
     A, B = cpu_sample_operands(w, seed, max(probe_rows, 256))
     dt, used = time_cpu_gemm(A, B, probe_rows)
     rate = 2.0 * probe_rows * N * K / max(dt, 1e-9)
