@@ -29,6 +29,11 @@ namespace b200gemm {
 #ifndef B200GEMM_EPIWARPS_N512
 #define B200GEMM_EPIWARPS_N512 16
 #endif
+// L2 sector promotion of every tensor map's loads (CUtensorMapL2promotion:
+// 0 none, 1 64 B, 2 128 B, 3 256 B).
+#ifndef B200GEMM_L2_PROMOTION
+#define B200GEMM_L2_PROMOTION 3
+#endif
 #ifndef B200GEMM_DEFAULT_ORDER
 #define B200GEMM_DEFAULT_ORDER 1
 #endif
@@ -135,7 +140,7 @@ bool encode_2d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer
   const CUresult r =
       encode(map, dtype, 2, const_cast<void*>(ptr), dims, strides, box,
              elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
-             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+             static_cast<CUtensorMapL2promotion>(B200GEMM_L2_PROMOTION), CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
