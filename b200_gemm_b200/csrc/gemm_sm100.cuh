@@ -925,7 +925,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
         acc_phase ^= 1u;
       }
     }
-    if (lane == 0) ptx::bulk_wait_group<0>();
+    if (lane == 0) ptx::bulk_wait_group_read<0>();  // staging reusable; the stores land before the kernel completes
     if (p.npeers > 0) __threadfence_system();  // peer copies visible before the kernel ends
     __syncwarp();
   }

@@ -310,7 +310,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       if (lane == 0 && row0 < p.M && col < p.N) {
         ptx::tma_store_2d(&map_c, cw, col, row0);
         ptx::bulk_commit_group();
-        ptx::bulk_wait_group<0>();
+        ptx::bulk_wait_group_read<0>();  // smem reusable; the stores land before the kernel completes
       }
       __syncwarp();
     }
