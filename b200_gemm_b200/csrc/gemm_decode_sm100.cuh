@@ -10,7 +10,10 @@
 // cluster of 2S CTAs.  Each CTA pair accumulates its K range in TMEM
 // (D[i][j] = sum_k B[n0 + i][k] * A[j][k] = C[j][n0 + i]); the pairs then
 // exchange fp32 partial sums through distributed shared memory (st.async,
-// counted on the receiver's mbarrier): CTA (pair p, half q) keeps the slice of
+// counted on the receiver's mbarrier; a partial slice is stored as
+// [column group of 4][B row][4 floats], so the 32 lanes of a warp, which hold
+// 32 consecutive B rows, write 512 contiguous bytes per store and read them
+// back bank-conflict free): CTA (pair p, half q) keeps the slice of
 // A rows j in [p * 128/S, (p+1) * 128/S), receives the other pairs' partials
 // of that slice, adds them, rounds to bf16 and writes C through a transposing
 // staging buffer.  No global workspace, one launch, N/256 * 2S CTAs.
@@ -48,8 +51,7 @@ struct DecodeCfg {
   static constexpr int kStageA = (kNT / 2) * kBlockK * 2;     // 8 KB: this CTA's 64 rows of A
   static constexpr int kStageBytes = kStageB + kStageA;
   static constexpr int kSliceRows = kNT / S;                 // rows of C each CTA finishes
-  static constexpr int kRowBytes = kSliceRows * 4;           // one B row's fp32 partial slice
-  static constexpr int kRecvSlotBytes = 128 * kRowBytes;
+  static constexpr int kRecvSlotBytes = 128 * kSliceRows * 4;  // [kSliceRows/4][128 rows][4] fp32
   static constexpr int kRecvBytes = (S - 1) * kRecvSlotBytes;
   static constexpr int kCWarpBytes = kSliceRows * 32 * 4;    // kSliceRows x 32 outputs (up to fp32) per warp
   static constexpr int kRWarpBytes = kSliceRows * 32 * 2;    // the same rows of the residual (bf16)
@@ -74,7 +76,6 @@ struct DecodeCfg {
   static_assert(kEnd - kFull <= kBarBytes, "barrier area");
   static constexpr int kSmemBytes = kEnd + 1024;
   static_assert(kSmemBytes <= 232448, "exceeds the 227 KB per-CTA shared memory limit");
-  static_assert(kRowBytes % 128 == 0, "partial rows are whole 128-byte swizzle groups");
 };
 
 // kind::f16, D f32, A = B = bf16 K-major, M = 256 (pair), N = 128.
@@ -232,8 +233,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         if (dst_pair == static_cast<int>(pair)) continue;
         const uint32_t dst_cta = static_cast<uint32_t>(dst_pair) * 2u + half;
         const int slot = static_cast<int>(pair) < dst_pair ? static_cast<int>(pair) : static_cast<int>(pair) - 1;
-        const uint32_t remote_row =
-            ptx::mapa(sRecv + slot * Cfg::kRecvSlotBytes + i * Cfg::kRowBytes, dst_cta);
+        const uint32_t remote_row = ptx::mapa(sRecv + slot * Cfg::kRecvSlotBytes + i * 16u, dst_cta);
         const uint32_t remote_bar = ptx::mapa(recv_bar, dst_cta);
 #pragma unroll 1
         for (int c = 0; c < Cfg::kSliceRows / 32; ++c) {
@@ -248,17 +248,22 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
           }
 #pragma unroll
           for (int g = 0; g < 8; ++g) {
-            const uint32_t chunk = (static_cast<uint32_t>(c * 8 + g)) ^ (i & 7u);
-            ptx::st_async_v4(remote_row + chunk * 16u, remote_bar, v[4 * g], v[4 * g + 1],
-                             v[4 * g + 2], v[4 * g + 3]);
+            ptx::st_async_v4(remote_row + static_cast<uint32_t>(c * 8 + g) * 2048u, remote_bar, v[4 * g],
+                             v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
           }
         }
       }
     }
     // 2. Finish this CTA's slice: own partial + received partials -> bf16 -> C.
+    // With a K split, the first 32 columns of the own partial are read from
+    // TMEM while the partners' slices are still arriving.
+    uint32_t v[32];
+    const bool early_ld = S > 1 && ok && have;
+    if (early_ld) ptx::tmem_ld_32x32b_x32(t_row + pair * Cfg::kSliceRows, v);
     if (ok && S > 1) {
       const bool got = ptx::mbar_wait(recv_bar, 0, wd, kSiteEpilogue, 1);
       ok = __all_sync(0xFFFFFFFFu, got);
+      if (!ok && early_ld) ptx::tmem_wait_ld();  // no TMEM load left in flight
     }
     if (ok) {
       const uint32_t cw = sC + (warp - 2u) * Cfg::kCWarpBytes;  // [kSliceRows][32] outputs
@@ -269,9 +274,8 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       }
 #pragma unroll 1
       for (int c = 0; c < Cfg::kSliceRows / 32; ++c) {
-        uint32_t v[32];
         if (have) {
-          ptx::tmem_ld_32x32b_x32(t_row + pair * Cfg::kSliceRows + c * 32, v);
+          if (c > 0 || S == 1) ptx::tmem_ld_32x32b_x32(t_row + pair * Cfg::kSliceRows + c * 32, v);
           ptx::tmem_wait_ld();
           ptx::reg_fence32(v);
         } else {
@@ -283,12 +287,11 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         for (int t = 0; t < 32; ++t) acc[t] = __uint_as_float(v[t]);
 #pragma unroll 1
         for (int slot = 0; slot < S - 1; ++slot) {
-          const uint32_t row = sRecv + slot * Cfg::kRecvSlotBytes + i * Cfg::kRowBytes;
+          const uint32_t row = sRecv + slot * Cfg::kRecvSlotBytes + i * 16u;
 #pragma unroll
           for (int g = 0; g < 8; ++g) {
-            const uint32_t chunk = (static_cast<uint32_t>(c * 8 + g)) ^ (i & 7u);
             uint32_t x0, x1, x2, x3;
-            ptx::ld_shared_v4(row + chunk * 16u, x0, x1, x2, x3);
+            ptx::ld_shared_v4(row + static_cast<uint32_t>(c * 8 + g) * 2048u, x0, x1, x2, x3);
             acc[4 * g] += __uint_as_float(x0);
             acc[4 * g + 1] += __uint_as_float(x1);
             acc[4 * g + 2] += __uint_as_float(x2);

@@ -49,8 +49,7 @@ struct SmallMCfg {
   static constexpr int kStageA = kNT * kBlockK * 2;          // 16 KB
   static constexpr int kStageBytes = kStageB + kStageA;
   static constexpr int kSliceRows = kNT / S;                 // rows of C each CTA finishes
-  static constexpr int kRowBytes = kSliceRows * 4;           // one B row's fp32 partial slice
-  static constexpr int kRecvSlotBytes = kRowsB * kRowBytes;
+  static constexpr int kRecvSlotBytes = kRowsB * kSliceRows * 4;  // [kSliceRows/4][128 rows][4] fp32
   static constexpr int kRecvBytes = (S - 1) * kRecvSlotBytes;
   static constexpr int kCWarpBytes = kSliceRows * 32 * 4;    // kSliceRows x 32 outputs (up to fp32) per warp
   static constexpr int kRWarpBytes = kSliceRows * 32 * 2;    // the same rows of the residual (bf16)
@@ -74,7 +73,6 @@ struct SmallMCfg {
   static_assert(kEnd - kFull <= kBarBytes, "barrier area");
   static constexpr int kSmemBytes = kEnd + 1024;
   static_assert(kSmemBytes <= 232448, "exceeds the 227 KB per-CTA shared memory limit");
-  static_assert(kRowBytes % 128 == 0, "partial rows are whole 128-byte swizzle groups");
 };
 
 // kind::f16, D f32, A = B = bf16 K-major, M = 128, N = 128.
@@ -237,8 +235,8 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       for (int dst = 0; dst < S; ++dst) {
         if (dst == static_cast<int>(rank)) continue;
         const int slot = static_cast<int>(rank) < dst ? static_cast<int>(rank) : static_cast<int>(rank) - 1;
-        const uint32_t remote_row = ptx::mapa(sRecv + slot * Cfg::kRecvSlotBytes + i * Cfg::kRowBytes,
-                                              static_cast<uint32_t>(dst));
+        const uint32_t remote_row =
+            ptx::mapa(sRecv + slot * Cfg::kRecvSlotBytes + i * 16u, static_cast<uint32_t>(dst));
         const uint32_t remote_bar = ptx::mapa(recv_bar, static_cast<uint32_t>(dst));
 #pragma unroll 1
         for (int c = 0; c < Cfg::kSliceRows / 32; ++c) {
@@ -253,17 +251,22 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
           }
 #pragma unroll
           for (int g = 0; g < 8; ++g) {
-            const uint32_t chunk = (static_cast<uint32_t>(c * 8 + g)) ^ (i & 7u);
-            ptx::st_async_v4(remote_row + chunk * 16u, remote_bar, v[4 * g], v[4 * g + 1],
-                             v[4 * g + 2], v[4 * g + 3]);
+            ptx::st_async_v4(remote_row + static_cast<uint32_t>(c * 8 + g) * 2048u, remote_bar, v[4 * g],
+                             v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
           }
         }
       }
     }
     // 2. Finish this CTA's slice: own partial + received partials -> bf16 -> C.
+    // With a K split, the first 32 columns of the own partial are read from
+    // TMEM while the partners' slices are still arriving.
+    uint32_t v[32];
+    const bool early_ld = S > 1 && ok && have;
+    if (early_ld) ptx::tmem_ld_32x32b_x32(t_row + rank * Cfg::kSliceRows, v);
     if (ok && S > 1) {
       const bool got = ptx::mbar_wait(recv_bar, 0, wd, kSiteEpilogue, 1);
       ok = __all_sync(0xFFFFFFFFu, got);
+      if (!ok && early_ld) ptx::tmem_wait_ld();  // no TMEM load left in flight
     }
     if (ok) {
       const uint32_t cw = sC + (warp - 2u) * Cfg::kCWarpBytes;  // [kSliceRows][32] outputs
@@ -274,9 +277,8 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       }
 #pragma unroll 1
       for (int c = 0; c < Cfg::kSliceRows / 32; ++c) {
-        uint32_t v[32];
         if (have) {
-          ptx::tmem_ld_32x32b_x32(t_row + rank * Cfg::kSliceRows + c * 32, v);
+          if (c > 0 || S == 1) ptx::tmem_ld_32x32b_x32(t_row + rank * Cfg::kSliceRows + c * 32, v);
           ptx::tmem_wait_ld();
           ptx::reg_fence32(v);
         } else {
@@ -288,12 +290,11 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         for (int t = 0; t < 32; ++t) acc[t] = __uint_as_float(v[t]);
 #pragma unroll 1
         for (int slot = 0; slot < S - 1; ++slot) {
-          const uint32_t row = sRecv + slot * Cfg::kRecvSlotBytes + i * Cfg::kRowBytes;
+          const uint32_t row = sRecv + slot * Cfg::kRecvSlotBytes + i * 16u;
 #pragma unroll
           for (int g = 0; g < 8; ++g) {
-            const uint32_t chunk = (static_cast<uint32_t>(c * 8 + g)) ^ (i & 7u);
             uint32_t x0, x1, x2, x3;
-            ptx::ld_shared_v4(row + chunk * 16u, x0, x1, x2, x3);
+            ptx::ld_shared_v4(row + static_cast<uint32_t>(c * 8 + g) * 2048u, x0, x1, x2, x3);
             acc[4 * g] += __uint_as_float(x0);
             acc[4 * g + 1] += __uint_as_float(x1);
             acc[4 * g + 2] += __uint_as_float(x2);
