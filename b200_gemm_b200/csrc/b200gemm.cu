@@ -370,16 +370,26 @@ double epilogue_cost(const b200gemm_epilogue* epi, int width) {
 using namespace b200gemm;
 
 // Device buffers, streams and events of b200gemm_bf16_nt_host (created on
-// first use, grown when a larger problem arrives).
+// first use, grown when a larger problem arrives).  Consecutive calls
+// alternate between two buffer sets, so a call's uploads start as soon as the
+// previous call's uploads end, while that call's last GEMM and copy-out
+// still run; a set is reused only after the call two back has finished with
+// it.
 struct HostStaging {
-  void* dA = nullptr;
-  void* dB = nullptr;
-  void* dC = nullptr;
-  size_t capA = 0, capB = 0, capC = 0;
+  struct Buffers {
+    void* dA = nullptr;
+    void* dB = nullptr;
+    void* dC = nullptr;
+    size_t capA = 0, capB = 0, capC = 0;
+    cudaEvent_t ev_read = nullptr;  // last GEMM of the last call on this set: dA, dB free
+    cudaEvent_t ev_done = nullptr;  // last copy-out of that call: dC free
+  };
+  Buffers set[2];
+  int next = 0;
   bool ready = false;
   cudaStream_t s_h2d = nullptr, s_mma = nullptr, s_d2h = nullptr;
   static constexpr int kMaxChunks = 16;
-  cudaEvent_t ev_start = nullptr, ev_b = nullptr, ev_done = nullptr;
+  cudaEvent_t ev_start = nullptr, ev_b = nullptr;
   cudaEvent_t ev_a[kMaxChunks] = {}, ev_c[kMaxChunks] = {};
 };
 
@@ -498,16 +508,19 @@ extern "C" void b200gemm_destroy(b200gemm_t h) {
     cudaFree(h->tail_counters);
     if (h->tail_event != nullptr) cudaEventDestroy(h->tail_event);
     HostStaging& st = h->staging;
-    cudaFree(st.dA);
-    cudaFree(st.dB);
-    cudaFree(st.dC);
+    for (auto& b : st.set) {
+      cudaFree(b.dA);
+      cudaFree(b.dB);
+      cudaFree(b.dC);
+      if (b.ev_read != nullptr) cudaEventDestroy(b.ev_read);
+      if (b.ev_done != nullptr) cudaEventDestroy(b.ev_done);
+    }
     if (st.ready) {
       cudaStreamDestroy(st.s_h2d);
       cudaStreamDestroy(st.s_mma);
       cudaStreamDestroy(st.s_d2h);
       cudaEventDestroy(st.ev_start);
       cudaEventDestroy(st.ev_b);
-      cudaEventDestroy(st.ev_done);
       for (int i = 0; i < HostStaging::kMaxChunks; ++i) {
         cudaEventDestroy(st.ev_a[i]);
         cudaEventDestroy(st.ev_c[i]);
@@ -1215,8 +1228,11 @@ bool prepare_staging(HostStaging& st) {
             cudaStreamCreateWithFlags(&st.s_mma, cudaStreamNonBlocking) == cudaSuccess &&
             cudaStreamCreateWithFlags(&st.s_d2h, cudaStreamNonBlocking) == cudaSuccess &&
             cudaEventCreateWithFlags(&st.ev_start, cudaEventDisableTiming) == cudaSuccess &&
-            cudaEventCreateWithFlags(&st.ev_b, cudaEventDisableTiming) == cudaSuccess &&
-            cudaEventCreateWithFlags(&st.ev_done, cudaEventDisableTiming) == cudaSuccess;
+            cudaEventCreateWithFlags(&st.ev_b, cudaEventDisableTiming) == cudaSuccess;
+  for (auto& b : st.set) {
+    ok = ok && cudaEventCreateWithFlags(&b.ev_read, cudaEventDisableTiming) == cudaSuccess &&
+         cudaEventCreateWithFlags(&b.ev_done, cudaEventDisableTiming) == cudaSuccess;
+  }
   for (int i = 0; ok && i < HostStaging::kMaxChunks; ++i) {
     ok = cudaEventCreateWithFlags(&st.ev_a[i], cudaEventDisableTiming) == cudaSuccess &&
          cudaEventCreateWithFlags(&st.ev_c[i], cudaEventDisableTiming) == cudaSuccess;
@@ -1241,11 +1257,20 @@ extern "C" int b200gemm_bf16_nt_host(b200gemm_t h, int M, int N, int K, const vo
   const size_t ldc_dev = (static_cast<size_t>(N) + 7) & ~static_cast<size_t>(7);
   const size_t bytesA = static_cast<size_t>(M) * K * 2, bytesB = static_cast<size_t>(N) * K * 2;
   const size_t bytesC = static_cast<size_t>(M) * ldc_dev * 2;
-  if (!prepare_staging(st) || !ensure_capacity(&st.dA, &st.capA, bytesA > 0 ? bytesA : 16) ||
-      !ensure_capacity(&st.dB, &st.capB, bytesB > 0 ? bytesB : 16) ||
-      !ensure_capacity(&st.dC, &st.capC, bytesC)) {
+  if (!prepare_staging(st)) return B200GEMM_ERR_CUDA;
+  HostStaging::Buffers& buf = st.set[st.next];
+  // A buffer about to be freed and grown may still be in use by the call
+  // two back: wait for it first (the usual case, same size, never waits).
+  if ((buf.capA < bytesA || buf.capB < bytesB || buf.capC < bytesC) &&
+      cudaEventSynchronize(buf.ev_done) != cudaSuccess) {
     return B200GEMM_ERR_CUDA;
   }
+  if (!ensure_capacity(&buf.dA, &buf.capA, bytesA > 0 ? bytesA : 16) ||
+      !ensure_capacity(&buf.dB, &buf.capB, bytesB > 0 ? bytesB : 16) ||
+      !ensure_capacity(&buf.dC, &buf.capC, bytesC)) {
+    return B200GEMM_ERR_CUDA;
+  }
+  st.next ^= 1;
   // Chunks: whole 256-row tiles, at most kMaxChunks of them, about 8 when M allows.
   const int tiles_m = (M + kTileM - 1) / kTileM;
   const int want = tiles_m < 8 ? tiles_m : 8;
@@ -1255,21 +1280,22 @@ extern "C" int b200gemm_bf16_nt_host(b200gemm_t h, int M, int N, int K, const vo
   if (chunks > HostStaging::kMaxChunks) return B200GEMM_ERR_TOO_LARGE;
 
   auto ok = [](cudaError_t e) { return e == cudaSuccess; };
-  // The staging buffers are reused: this call's copies wait for the previous
-  // call's last copy-out (a never-recorded event is already complete).
-  if (!ok(cudaStreamWaitEvent(st.s_h2d, st.ev_done, 0)) || !ok(cudaStreamWaitEvent(st.s_mma, st.ev_done, 0)))
+  // This set was last used by the call two back: the uploads wait for its
+  // last GEMM, the GEMMs (which write dC) for its last copy-out.  A
+  // never-recorded event is already complete.
+  if (!ok(cudaStreamWaitEvent(st.s_h2d, buf.ev_read, 0)) || !ok(cudaStreamWaitEvent(st.s_mma, buf.ev_done, 0)))
     return B200GEMM_ERR_CUDA;
   if (!ok(cudaEventRecord(st.ev_start, stream)) || !ok(cudaStreamWaitEvent(st.s_h2d, st.ev_start, 0)) ||
       !ok(cudaStreamWaitEvent(st.s_mma, st.ev_start, 0)) ||
       !ok(cudaStreamWaitEvent(st.s_d2h, st.ev_start, 0))) {
     return B200GEMM_ERR_CUDA;
   }
-  if (bytesB > 0 && !ok(cudaMemcpyAsync(st.dB, hB, bytesB, cudaMemcpyHostToDevice, st.s_h2d)))
+  if (bytesB > 0 && !ok(cudaMemcpyAsync(buf.dB, hB, bytesB, cudaMemcpyHostToDevice, st.s_h2d)))
     return B200GEMM_ERR_CUDA;
   if (!ok(cudaEventRecord(st.ev_b, st.s_h2d)) || !ok(cudaStreamWaitEvent(st.s_mma, st.ev_b, 0)))
     return B200GEMM_ERR_CUDA;
-  auto* dA = static_cast<uint8_t*>(st.dA);
-  auto* dC = static_cast<uint8_t*>(st.dC);
+  auto* dA = static_cast<uint8_t*>(buf.dA);
+  auto* dC = static_cast<uint8_t*>(buf.dC);
   const auto* srcA = static_cast<const uint8_t*>(hA);
   auto* dstC = static_cast<uint8_t*>(hC);
   for (int i = 0; i < chunks; ++i) {
@@ -1282,7 +1308,7 @@ extern "C" int b200gemm_bf16_nt_host(b200gemm_t h, int M, int N, int K, const vo
     if (!ok(cudaEventRecord(st.ev_a[i], st.s_h2d)) ||
         !ok(cudaStreamWaitEvent(st.s_mma, st.ev_a[i], 0)))
       return B200GEMM_ERR_CUDA;
-    const int rc = gemm_device(h, rows, N, K, dA + a_off, st.dB, dC + r0 * ldc_dev * 2,
+    const int rc = gemm_device(h, rows, N, K, dA + a_off, buf.dB, dC + r0 * ldc_dev * 2,
                                static_cast<int>(ldc_dev), st.s_mma, /*allow_small_m=*/M <= 128);
     if (rc != B200GEMM_OK) return rc;
     if (!ok(cudaEventRecord(st.ev_c[i], st.s_mma)) ||
@@ -1292,7 +1318,8 @@ extern "C" int b200gemm_bf16_nt_host(b200gemm_t h, int M, int N, int K, const vo
                               static_cast<size_t>(rows), cudaMemcpyDeviceToHost, st.s_d2h)))
       return B200GEMM_ERR_CUDA;
   }
-  if (!ok(cudaEventRecord(st.ev_done, st.s_d2h)) || !ok(cudaStreamWaitEvent(stream, st.ev_done, 0)))
+  if (!ok(cudaEventRecord(buf.ev_read, st.s_mma)) || !ok(cudaEventRecord(buf.ev_done, st.s_d2h)) ||
+      !ok(cudaStreamWaitEvent(stream, buf.ev_done, 0)))
     return B200GEMM_ERR_CUDA;
   return B200GEMM_OK;
 }

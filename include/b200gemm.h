@@ -101,7 +101,11 @@ int b200gemm_bf16_nt_epilogue(b200gemm_t handle, int M, int N, int K, const void
  * 256-row tiles on separate streams, so the copy of chunk i+1, the GEMM of
  * chunk i and the copy-out of chunk i-1 overlap.  Asynchronous with respect
  * to the host: completion is ordered on `stream`, and the host buffers must
- * stay valid until then.  Calls on one handle are serialised.  ldc is the
+ * stay valid until then.  Consecutive calls alternate between two sets of
+ * device buffers, so a call on another stream uploads its operands while the
+ * previous call's last GEMM and copy-out still run (a call on the same stream
+ * starts after the previous one completes, as stream order requires).  Calls
+ * on one handle are enqueued one at a time.  ldc is the
  * host row pitch of C (>= N); K % 8 == 0.  No reference counterpart (the
  * reference bench copies synchronously, matmul_b200.cu:80-83, 107-110). */
 int b200gemm_bf16_nt_host(b200gemm_t handle, int M, int N, int K, const void* A, const void* B,

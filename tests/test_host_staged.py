@@ -46,3 +46,25 @@ def test_host_path_twice_and_host_pitch(gpu_handle):
         ref = gpu_handle.bf16_nt(_host(A_bits, False).cuda(), _host(B_bits, False).cuda())
         torch.cuda.synchronize()
         assert torch.equal(wide[:, :N].contiguous().view(torch.int16), ref.cpu().view(torch.int16))
+
+
+def test_host_path_interleaved_streams(gpu_handle):
+    """Calls alternating between two streams overlap through the two staging
+    sets; shapes change mid-sequence (the larger one grows a set while the
+    other may still be in flight), and every result matches the device path."""
+    shapes = [(1024, 768, 512), (1024, 768, 512), (2304, 1280, 768), (1024, 768, 512), (512, 256, 128),
+              (2304, 1280, 768)]
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    jobs = []
+    for i, (M, N, K) in enumerate(shapes):
+        A_bits, B_bits = data.host_operands(M, N, K, "normal", seed=100 + i)
+        hA, hB = _host(A_bits, True), _host(B_bits, True)
+        out = torch.full((M, N), float("nan"), dtype=torch.bfloat16).pin_memory()
+        gpu_handle.bf16_nt_host(hA, hB, out=out, stream=streams[i % 2])
+        jobs.append((hA, hB, out))
+    for s in streams:
+        s.synchronize()
+    for hA, hB, out in jobs:
+        ref = gpu_handle.bf16_nt(hA.cuda(), hB.cuda())
+        torch.cuda.synchronize()
+        assert torch.equal(out.view(torch.int16), ref.cpu().view(torch.int16))
