@@ -42,6 +42,8 @@ WORKLOADS = {
     "square16384": dict(M=16384, N=16384, K=16384, dist="normal", scaling="strong"),
     "mlp": dict(M=16384, N=14336, K=4096, dist="mlp", scaling="strong"),
     "decode": dict(M=128, N=8192, K=8192, dist="normal", scaling="strong", bound="hbm"),
+    # the MLP config's down projection (K = 14336 -> N = 4096) at 128 tokens
+    "decode_down": dict(M=128, N=4096, K=14336, dist="normal", scaling="strong", bound="hbm"),
     "square512": dict(M=512, N=512, K=512, dist="normal", scaling="strong"),
 }
 METRIC = "bf16 GEMM TFLOPS @8192^3 (1 GPU) + N-GPU aggregate"
