@@ -207,6 +207,14 @@ class Gemm:
         """-1/1: use the small-M kernel for eligible shapes (default); 0: never."""
         _lib.check(self._lib.b200gemm_set_small_m(self._h, int(mode)), "b200gemm_set_small_m")
 
+    def set_pdl(self, mode: int) -> None:
+        """Launch overlap of the small-M kernels with the previous kernel on
+        the stream: _lib.PDL_OFF (default), PDL_ON (setup overlaps; every
+        global access waits for the previous kernel) or PDL_WEIGHTS_EARLY (B
+        also starts streaming before that wait; the previous kernel must not
+        write B)."""
+        _lib.check(self._lib.b200gemm_set_pdl(self._h, int(mode)), "b200gemm_set_pdl")
+
     def small_m_split(self, M: int, N: int, K: int) -> int:
         """K split of the small-M kernel for this shape, or 0 if the tiled kernel runs."""
         return int(self._lib.b200gemm_small_m_split(self._h, M, N, K))

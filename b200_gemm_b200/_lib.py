@@ -25,6 +25,7 @@ ORDER_BANDS = 1
 
 ACT_NONE, ACT_RELU, ACT_GELU, ACT_GELU_TANH, ACT_SILU = 0, 1, 2, 3, 4
 OUT_BF16, OUT_F32, OUT_E4M3 = 0, 1, 2
+PDL_OFF, PDL_ON, PDL_WEIGHTS_EARLY = 0, 1, 2
 
 _c_int, _c_uint, _c_ull, _vp = ctypes.c_int, ctypes.c_uint, ctypes.c_ulonglong, ctypes.c_void_p
 
@@ -66,6 +67,7 @@ SIGNATURES = {
     "b200gemm_set_tile_width": (_c_int, [_vp, _c_int]),
     "b200gemm_tile_width_for": (_c_int, [_vp, _c_int, _c_int, _c_int]),
     "b200gemm_set_small_m": (_c_int, [_vp, _c_int]),
+    "b200gemm_set_pdl": (_c_int, [_vp, _c_int]),
     "b200gemm_small_m_split": (_c_int, [_vp, _c_int, _c_int, _c_int]),
     "b200gemm_set_schedule": (_c_int, [_vp, _c_int, _c_int]),
     "b200gemm_schedule_host": (_c_int, [_c_uint, _c_uint, _c_int, _c_int, ctypes.POINTER(_c_uint)]),

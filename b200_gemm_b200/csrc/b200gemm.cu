@@ -259,7 +259,7 @@ cudaError_t launch_smallm1(cudaStream_t stream, const CUtensorMap& ma, const CUt
                            const CUtensorMap& mc, const CUtensorMap& mr, const SmallMParams& p) {
   const unsigned clusters = static_cast<unsigned>((p.N + 127) / 128);
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = Cfg::kSplit;
   attr[0].val.clusterDim.y = 1;
@@ -270,6 +270,11 @@ cudaError_t launch_smallm1(cudaStream_t stream, const CUtensorMap& ma, const CUt
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (p.pdl != kPdlOff) {
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.numAttrs = 2;
+  }
   return cudaLaunchKernelEx(&cfg, gemm_bf16_nt_smallm1_sm100<Cfg>, ma, mb, mc, mr, p);
 }
 
@@ -278,7 +283,7 @@ cudaError_t launch_decode(cudaStream_t stream, const CUtensorMap& ma, const CUte
                           const CUtensorMap& mc, const CUtensorMap& mr, const DecodeParams& p) {
   const unsigned clusters = static_cast<unsigned>((p.N + 255) / 256);
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = Cfg::kClusterSize;
   attr[0].val.clusterDim.y = 1;
@@ -289,6 +294,11 @@ cudaError_t launch_decode(cudaStream_t stream, const CUtensorMap& ma, const CUte
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (p.pdl != kPdlOff) {
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.numAttrs = 2;
+  }
   return cudaLaunchKernelEx(&cfg, gemm_bf16_nt_decode_sm100<Cfg>, ma, mb, mc, mr, p);
 }
 
@@ -403,6 +413,7 @@ struct b200gemm_handle {
   int smallm1_clusters[5] = {};       // [S]: the same for the single-CTA small-M kernel
   int tile_width = 0;         // 0 = choose per call, else one of kWidths
   int small_m = -1;           // small-M kernel: -1 or 1 = use it when eligible, 0 = never
+  int pdl = 0;                // B200GEMM_PDL_* for the small-M kernels
   unsigned int* status_dev = nullptr;
   unsigned long long timeout_ns = kDefaultTimeoutNs;
   int order = B200GEMM_DEFAULT_ORDER;      // tile order (schedule.cuh)
@@ -789,7 +800,8 @@ SmallMPlan smallm_plan(const b200gemm_handle* h, int M, int N, int K) {
 }
 
 int run_smallm1(b200gemm_t h, int split, int M, int N, int K, const void* A, const void* B, void* C,
-                int ldc, cudaStream_t stream, unsigned long long timeout_ns, const b200gemm_epilogue* epi) {
+                int ldc, cudaStream_t stream, unsigned long long timeout_ns, int pdl,
+                const b200gemm_epilogue* epi) {
   const uint64_t k = static_cast<uint64_t>(K);
   CUtensorMap ma, mb, mc, mr;
   const uint32_t slice_rows = static_cast<uint32_t>(128 / split);
@@ -809,6 +821,7 @@ int run_smallm1(b200gemm_t h, int split, int M, int N, int K, const void* A, con
   p.kb_per_split = (p.num_kb + split - 1) / split;
   p.status = h->status_dev;
   p.timeout_ns = timeout_ns;
+  p.pdl = pdl;
   cudaError_t e;
   if (split == 4) e = launch_smallm1<SmallMCfg<4>>(stream, ma, mb, mc, mr, p);
   else if (split == 2) e = launch_smallm1<SmallMCfg<2>>(stream, ma, mb, mc, mr, p);
@@ -817,7 +830,8 @@ int run_smallm1(b200gemm_t h, int split, int M, int N, int K, const void* A, con
 }
 
 int run_decode(b200gemm_t h, int split, int M, int N, int K, const void* A, const void* B, void* C,
-               int ldc, cudaStream_t stream, unsigned long long timeout_ns, const b200gemm_epilogue* epi) {
+               int ldc, cudaStream_t stream, unsigned long long timeout_ns, int pdl,
+               const b200gemm_epilogue* epi) {
   const uint64_t k = static_cast<uint64_t>(K);
   CUtensorMap ma, mb, mc, mr;
   const uint32_t slice_rows = static_cast<uint32_t>(128 / split);
@@ -837,6 +851,7 @@ int run_decode(b200gemm_t h, int split, int M, int N, int K, const void* A, cons
   p.kb_per_split = (p.num_kb + split - 1) / split;
   p.status = h->status_dev;
   p.timeout_ns = timeout_ns;
+  p.pdl = pdl;
   cudaError_t e;
   if (split == 4) e = launch_decode<DecodeCfg<4>>(stream, ma, mb, mc, mr, p);
   else if (split == 2) e = launch_decode<DecodeCfg<2>>(stream, ma, mb, mc, mr, p);
@@ -856,6 +871,17 @@ extern "C" int b200gemm_set_small_m(b200gemm_t h, int mode) {
   if (h == nullptr || mode < -1 || mode > 1) return B200GEMM_ERR_INVALID_ARG;
   std::lock_guard<std::mutex> lock(h->mu);
   h->small_m = mode;
+  return B200GEMM_OK;
+}
+
+static_assert(B200GEMM_PDL_OFF == kPdlOff && B200GEMM_PDL_ON == kPdlOn &&
+                  B200GEMM_PDL_WEIGHTS_EARLY == kPdlWeightsEarly,
+              "header and kernel agree on the launch-overlap modes");
+
+extern "C" int b200gemm_set_pdl(b200gemm_t h, int mode) {
+  if (h == nullptr || mode < B200GEMM_PDL_OFF || mode > B200GEMM_PDL_WEIGHTS_EARLY) return B200GEMM_ERR_INVALID_ARG;
+  std::lock_guard<std::mutex> lock(h->mu);
+  h->pdl = mode;
   return B200GEMM_OK;
 }
 
@@ -978,15 +1004,17 @@ int gemm_device(b200gemm_t h, int M, int N, int K, const void* A, const void* B,
   // Small M: stream B with every SM (operands swapped, K split in-cluster).
   SmallMPlan sm{0, 0};
   unsigned long long decode_timeout;
+  int pdl;
   // Their C stores clip N in 16-byte units: e4m3 output needs N % 16 == 0.
   const bool smallm_ok = allow_small_m && npeers == 0 && (c_type != B200GEMM_OUT_E4M3 || (N % 16) == 0);
   {
     std::lock_guard<std::mutex> lock(h->mu);
     if (smallm_ok && h->small_m != 0) sm = smallm_plan(h, M, N, K);
     decode_timeout = h->timeout_ns;
+    pdl = h->pdl;
   }
-  if (sm.kind == 2) return run_decode(h, sm.split, M, N, K, A, B, C, ldc, stream, decode_timeout, epi);
-  if (sm.kind == 3) return run_smallm1(h, sm.split, M, N, K, A, B, C, ldc, stream, decode_timeout, epi);
+  if (sm.kind == 2) return run_decode(h, sm.split, M, N, K, A, B, C, ldc, stream, decode_timeout, pdl, epi);
+  if (sm.kind == 3) return run_smallm1(h, sm.split, M, N, K, A, B, C, ldc, stream, decode_timeout, pdl, epi);
 
   CUtensorMap ma, mb, mc;
   const uint32_t* sched = nullptr;

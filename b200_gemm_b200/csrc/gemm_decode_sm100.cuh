@@ -38,6 +38,7 @@ struct DecodeParams {
   unsigned int* status;
   unsigned long long timeout_ns;
   EpiArgs epi;       // fused epilogue (identity: no flags, act none, bf16, alpha 1)
+  int pdl;           // launch overlap with the previous kernel: kPdl*
 };
 
 template <int S>
@@ -150,8 +151,23 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       const uint64_t policy_b = ptx::policy_evict_first();  // B is read once
       const uint64_t policy_a = ptx::policy_evict_last();   // A is read by every cluster
       const uint32_t full_leader0 = ptx::mapa(full0, rank & ~1u);
-      uint32_t stage = 0, phase = 0;
-      for (int kb = kb_begin; kb < kb_end; ++kb) {
+      // With kPdlWeightsEarly the first ring of B (the weights, which the
+      // previous kernel does not write) streams in before that kernel has
+      // finished; A and everything after wait for it.
+      const int pre = p.pdl == kPdlWeightsEarly ? min(STAGES, nkb) : 0;
+      for (int s = 0; s < pre; ++s) {
+        if (leader) ptx::mbar_arrive_expect_tx(full0 + 8 * s, 2 * Cfg::kStageBytes);
+        ptx::tma_load_2d_cg2(sB + s * Cfg::kStageB, &map_b, full_leader0 + 8 * s, (kb_begin + s) * kBlockK,
+                             n0 + static_cast<int>(half) * 128, policy_b);
+      }
+      ptx::griddep_wait();
+      for (int s = 0; s < pre; ++s) {
+        ptx::tma_load_2d_cg2(sA + s * Cfg::kStageA, &map_a, full_leader0 + 8 * s, (kb_begin + s) * kBlockK,
+                             static_cast<int>(half) * (Cfg::kNT / 2), policy_a);
+      }
+      uint32_t stage = pre == STAGES ? 0u : static_cast<uint32_t>(pre);
+      uint32_t phase = pre == STAGES ? 1u : 0u;
+      for (int kb = kb_begin + pre; kb < kb_end; ++kb) {
         if (!ptx::mbar_wait(empty0 + 8 * stage, phase ^ 1u, wd, kSiteProducer, 0)) break;
         if (leader) ptx::mbar_arrive_expect_tx(full0 + 8 * stage, 2 * Cfg::kStageBytes);
         const uint32_t fb = full_leader0 + 8 * stage;
@@ -166,6 +182,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       }
     }
     __syncwarp();
+    if (p.pdl != kPdlOff) ptx::griddep_launch_dependents();
   } else if (warp == 1) {
     // ----------------------------------------------------------------- MMA
     if (leader && lane == 0) {
@@ -202,6 +219,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       ptx::mbar_wait_drain(drain, 0, dwd, kSiteDrain);
     }
     __syncwarp();
+    if (p.pdl != kPdlOff) ptx::griddep_launch_dependents();
   } else {
     // ------------------------------------------------------------ epilogue
     const uint32_t quarter = warp & 3u;             // TMEM lanes = rows of B this warp holds
@@ -209,11 +227,13 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     const uint32_t t_row = tmem_base + ((quarter * 32u) << 16);
     const bool have = nkb > 0;                      // a pair with no K blocks contributes zeros
     bool ok = true;
+    ptx::griddep_wait();  // bias, residual and C may belong to the previous kernel
     if (have) {
       const bool got = ptx::mbar_wait(tfull, 0, wd, kSiteEpilogue, 0);
       ok = __all_sync(0xFFFFFFFFu, got);
       ptx::tc_fence_after();
     }
+    if (p.pdl != kPdlOff) ptx::griddep_launch_dependents();
     // The residual rows and columns this warp adds at the end: one TMA load
     // into the B stages (free once the MMAs are done), in flight during the
     // exchange below.  Rows past M and columns past N read as zeros.

@@ -36,6 +36,7 @@ struct SmallMParams {
   unsigned int* status;
   unsigned long long timeout_ns;
   EpiArgs epi;       // fused epilogue (identity: no flags, act none, bf16, alpha 1)
+  int pdl;           // launch overlap with the previous kernel: kPdl*
 };
 
 template <int S>
@@ -144,11 +145,20 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
   ptx::tc_fence_before();
   ptx::cluster_arrive();
   if (warp == 0 && lane == 0) {
+    // With kPdlWeightsEarly B (the weights, which the previous kernel does
+    // not write) streams in before that kernel has finished; A waits for it.
+    const bool b_first = p.pdl == kPdlWeightsEarly;
+    if (!b_first) ptx::griddep_wait();
     for (int s = 0; s < early; ++s) {
       const int kb = kb_begin + s;
       ptx::mbar_arrive_expect_tx(full0 + 8 * s, Cfg::kStageBytes);
       ptx::tma_load_2d(sB + s * Cfg::kStageB, &map_b, full0 + 8 * s, kb * kBlockK, n0, policy_b);
-      ptx::tma_load_2d(sA + s * Cfg::kStageA, &map_a, full0 + 8 * s, kb * kBlockK, 0, policy_a);
+      if (!b_first) ptx::tma_load_2d(sA + s * Cfg::kStageA, &map_a, full0 + 8 * s, kb * kBlockK, 0, policy_a);
+    }
+    if (b_first) {
+      ptx::griddep_wait();
+      for (int s = 0; s < early; ++s)
+        ptx::tma_load_2d(sA + s * Cfg::kStageA, &map_a, full0 + 8 * s, (kb_begin + s) * kBlockK, 0, policy_a);
     }
   }
   ptx::cluster_wait();
@@ -173,6 +183,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       }
     }
     __syncwarp();
+    if (p.pdl != kPdlOff) ptx::griddep_launch_dependents();
   } else if (warp == 1) {
     // ----------------------------------------------------------------- MMA
     if (lane == 0) {
@@ -205,6 +216,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       ptx::mbar_wait_drain(drain, 0, dwd, kSiteDrain);
     }
     __syncwarp();
+    if (p.pdl != kPdlOff) ptx::griddep_launch_dependents();
   } else {
     // ------------------------------------------------------------ epilogue
     const uint32_t quarter = warp & 3u;             // TMEM lanes = rows of B this warp holds
@@ -212,11 +224,13 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     const uint32_t t_row = tmem_base + ((quarter * 32u) << 16);
     const bool have = nkb > 0;                      // a CTA with no K blocks contributes zeros
     bool ok = true;
+    ptx::griddep_wait();  // bias, residual and C may belong to the previous kernel
     if (have) {
       const bool got = ptx::mbar_wait(tfull, 0, wd, kSiteEpilogue, 0);
       ok = __all_sync(0xFFFFFFFFu, got);
       ptx::tc_fence_after();
     }
+    if (p.pdl != kPdlOff) ptx::griddep_launch_dependents();
     // The residual rows and columns this warp adds at the end: one TMA load
     // into the B stages (free once the MMAs are done), in flight during the
     // exchange below.  Rows past M and columns past N read as zeros.

@@ -41,9 +41,12 @@ WORKLOADS = {
     "square8192": dict(M=8192, N=8192, K=8192, dist="uniform", scaling="weak"),
     "square16384": dict(M=16384, N=16384, K=16384, dist="normal", scaling="strong"),
     "mlp": dict(M=16384, N=14336, K=4096, dist="mlp", scaling="strong"),
-    "decode": dict(M=128, N=8192, K=8192, dist="normal", scaling="strong", bound="hbm"),
+    # Decode shapes run as a decoder runs them: back to back, each step on the
+    # next of `weights` weight matrices (B), whose total exceeds twice L2, with
+    # the small-M kernels' launch overlap (B200GEMM_PDL_WEIGHTS_EARLY).
+    "decode": dict(M=128, N=8192, K=8192, dist="normal", scaling="strong", bound="hbm", weights=8),
     # the MLP config's down projection (K = 14336 -> N = 4096) at 128 tokens
-    "decode_down": dict(M=128, N=4096, K=14336, dist="normal", scaling="strong", bound="hbm"),
+    "decode_down": dict(M=128, N=4096, K=14336, dist="normal", scaling="strong", bound="hbm", weights=8),
     "square512": dict(M=512, N=512, K=512, dist="normal", scaling="strong"),
 }
 METRIC = "bf16 GEMM TFLOPS @8192^3 (1 GPU) + N-GPU aggregate"
@@ -171,23 +174,28 @@ def shard_shape(w, world: int, rank: int):
     return M, n1 - n0, K, n0
 
 
-def time_steps(torch, step, steps, flush, stream, dev, barrier, per_step=None):
+def time_steps(torch, step, steps, flush, stream, dev, barrier, per_step=None, between=True):
     """Device milliseconds for `steps` calls of `step` on `stream`.
 
     Operands far larger than L2: back-to-back steps, an event between every
-    two (the total runs from the first event to the last).  Otherwise a
-    256 MB buffer is overwritten before every step (outside the timed pair,
-    per-step events) so no step starts with its operands in L2.  The
-    per-step times go into `per_step` when a list is given."""
+    two (the total runs from the first event to the last), or with
+    between=False only around the whole run (an event between two launches
+    would keep the second from overlapping the first).  Otherwise a 256 MB
+    buffer is overwritten before every step (outside the timed pair, per-step
+    events) so no step starts with its operands in L2.  The per-step times go
+    into `per_step` when a list is given."""
     if not flush:
-        evs = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1 if between else 2)]
         barrier()
         evs[0].record(stream)
         for i in range(steps):
             step()
-            evs[i + 1].record(stream)
+            if between:
+                evs[i + 1].record(stream)
+        if not between:
+            evs[1].record(stream)
         barrier()
-        if per_step is not None:
+        if per_step is not None and between:
             per_step.extend(evs[i].elapsed_time(evs[i + 1]) for i in range(steps))
         return evs[0].elapsed_time(evs[-1])
     scratch = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
@@ -423,18 +431,27 @@ def run_ours(args, w):
     # Operands: A replicated (same seed everywhere), B rows [n0, n0 + Nl).
     A, _ = data.device_operands(M, 8, K, w["dist"], seed=args.seed, device=dev)
     _, B = data.device_operands(8, Nl, K, w["dist"], seed=args.seed + 1 + n0, device=dev)
+    # Decode workloads: step i multiplies by weight matrix i mod nw.
+    nw = w.get("weights", 1)
+    Bs = [B] + [data.device_operands(8, Nl, K, w["dist"], seed=args.seed + 1 + n0 + 7919 * j, device=dev)[1]
+                for j in range(1, nw)]
     C = torch.empty(M, Nl, dtype=torch.bfloat16, device=dev)
     gemm = Gemm(local)
+    if nw > 1:
+        gemm.set_pdl(_lib.PDL_WEIGHTS_EARLY)  # B is never written by the kernel before
     if args.tile_width:
         gemm.set_tile_width(args.tile_width)
     if args.order != "default":
         gemm.set_schedule(_lib.ORDER_HILBERT if args.order == "hilbert" else _lib.ORDER_BANDS, args.band)
     stream = torch.cuda.current_stream(dev)
     sptr = int(stream.cuda_stream)
-    a_ptr, b_ptr, c_ptr = A.data_ptr(), B.data_ptr(), C.data_ptr()
+    a_ptr, c_ptr = A.data_ptr(), C.data_ptr()
+    b_ptrs = [b.data_ptr() for b in Bs]
+    turn = [0]
 
     def step():
-        rc = gemm.bf16_nt_ptr(M, Nl, K, a_ptr, b_ptr, c_ptr, Nl, sptr)
+        rc = gemm.bf16_nt_ptr(M, Nl, K, a_ptr, b_ptrs[turn[0] % nw], c_ptr, Nl, sptr)
+        turn[0] += 1
         if rc != _lib.OK:
             raise RuntimeError(_lib.strerror(rc))
 
@@ -442,10 +459,11 @@ def run_ours(args, w):
     if library_arm:
         # Comparison arm: the same operands through cuBLASLt (no kernel of ours runs).
         torch.backends.cuda.preferred_blas_library("cublaslt")
-        Bt = B.t()
+        Bts = [b.t() for b in Bs]
 
         def step():  # noqa: F811
-            torch.matmul(A, Bt, out=C)
+            torch.matmul(A, Bts[turn[0] % nw], out=C)
+            turn[0] += 1
 
     for _ in range(max(3, args.warmup)):
         step()
@@ -454,11 +472,12 @@ def run_ours(args, w):
     if st != _lib.OK:
         raise RuntimeError(f"device status {st} {detail}")
 
-    operand_bytes = (M * K + Nl * K) * 2
+    operand_bytes = (M * K + nw * Nl * K) * 2
     flush = operand_bytes < 2 * L2_BYTES
+    between = nw == 1
     with ClockSampler(local) as clocks:
         step_ms = []
-        ms = time_steps(torch, step, args.steps, flush, stream, dev, barrier, step_ms)
+        ms = time_steps(torch, step, args.steps, flush, stream, dev, barrier, step_ms, between)
     st, detail = gemm.last_device_status()
     if st != _lib.OK:
         raise RuntimeError(f"device status {st} {detail}")
@@ -477,12 +496,17 @@ def run_ours(args, w):
     if not args.no_cublas and not library_arm:
         torch.backends.cuda.preferred_blas_library("cublaslt")
         Cr = torch.empty_like(C)
-        Bt = B.t()
-        cub_step = lambda: torch.matmul(A, Bt, out=Cr)  # noqa: E731
+        Bts = [b.t() for b in Bs]
+        cturn = [0]
+
+        def cub_step():
+            torch.matmul(A, Bts[cturn[0] % nw], out=Cr)
+            cturn[0] += 1
+
         for _ in range(max(3, args.warmup)):
             cub_step()
         barrier()
-        cms = time_steps(torch, cub_step, args.steps, flush, stream, dev, barrier)
+        cms = time_steps(torch, cub_step, args.steps, flush, stream, dev, barrier, None, between)
         extra["cublaslt"] = {"value": flops_rank / (cms / 1e3 / args.steps) / 1e12, "unit": "TFLOPS",
                              "per_gpu": True, "how": "torch.matmul, preferred_blas_library=cublaslt; "
                                                      "timed exactly like `value` (same L2 rule)"}
@@ -490,7 +514,8 @@ def run_ours(args, w):
 
     # ------------------------------- GEMM + bias + activation in the epilogue
     if args.epilogue and not library_arm:
-        extra["epilogue"] = time_epilogue(gemm, torch, A, B, C, args, flush, stream, dev, barrier,
+        one_b_flush = (M * K + Nl * K) * 2 < 2 * L2_BYTES  # this leg uses one B
+        extra["epilogue"] = time_epilogue(gemm, torch, A, B, C, args, one_b_flush, stream, dev, barrier,
                                           flops_rank)
 
     # ---------------------------------------- optional all-gather of C shards
@@ -546,7 +571,7 @@ def run_ours(args, w):
         e2e = run_e2e(gemm, torch, dev, stream, M, Nl, K, A, B, args, barrier, distributed, world)
         extra["e2e"] = e2e
 
-    del A, B, C
+    del A, B, C, Bs
     info = gemm.device_info()
     result = None
     if rank == 0:
@@ -564,13 +589,18 @@ def run_ours(args, w):
                        "l2": ("operands %.0f MB > 2x L2 (126 MB): back-to-back steps, no flush"
                               % (operand_bytes / 1e6)) if not flush else
                              ("operands %.0f MB < 2x L2: 256 MB L2 flush before each step, "
-                              "per-step CUDA events" % (operand_bytes / 1e6))},
+                              "per-step CUDA events" % (operand_bytes / 1e6)),
+                       **({"weights": f"{nw} weight matrices B rotate, step i uses B[i mod {nw}]; CUDA events "
+                                      "only around the whole run",
+                           "launch_overlap": None if library_arm else "B200GEMM_PDL_WEIGHTS_EARLY"}
+                          if nw > 1 else {})},
             "gpu_launches": 0 if library_arm else args.steps,
             "launch": launch_shape(gemm, M, Nl, K, info, library_arm),
             "roofline": roofline(w, M, Nl, K, ms / args.steps, peaks, peak_kind, traffic),
-            "per_launch_ms": {"mean": ms / args.steps, "median": statistics.median(step_ms),
-                              "best": min(step_ms), "worst": max(step_ms),
-                              "how": "CUDA events between consecutive launches (rank 0)"},
+            "per_launch_ms": ({"mean": ms / args.steps, "median": statistics.median(step_ms),
+                               "best": min(step_ms), "worst": max(step_ms),
+                               "how": "CUDA events between consecutive launches (rank 0)"} if step_ms else
+                              {"mean": ms / args.steps, "how": "events around the whole run only"}),
             "clocks": clocks.summary(),
         }
         result.update(extra)

@@ -201,6 +201,23 @@ int b200gemm_tile_width_for(b200gemm_t handle, int M, int N, int K);
  * 0: always use the tiled kernel.  The reference has no small-M path. */
 int b200gemm_set_small_m(b200gemm_t handle, int mode);
 
+/* Launch overlap for the small-M kernels (programmatic dependent launch).
+ * OFF (default): a call starts after the previous work on the stream.
+ * ON: the kernel may be scheduled while the previous kernel on the stream is
+ *   still running; it sets up (barriers, tensor memory) and then waits for
+ *   that kernel to complete before any access to global memory, and it lets
+ *   the next kernel launched this way start its own setup while it finishes.
+ * WEIGHTS_EARLY: as ON, and the first ring of B (the weights) is requested
+ *   before that wait, so streaming B overlaps the previous kernel's tail.
+ *   The caller guarantees that the previous kernel does not write B.
+ * Other kernels and work on the stream (copies, events) are unaffected, and
+ * the tiled kernel always launches without overlap.  The reference launches
+ * one kernel per call with no overlap (matmul_1.cuh:416). */
+#define B200GEMM_PDL_OFF 0
+#define B200GEMM_PDL_ON 1
+#define B200GEMM_PDL_WEIGHTS_EARLY 2
+int b200gemm_set_pdl(b200gemm_t handle, int mode);
+
 /* The K split (1, 2 or 4) the small-M kernel (pair or single-CTA form, see
  * b200gemm_plan) would use for this shape on this handle, or 0 when the
  * tiled kernel would run. */

@@ -76,6 +76,7 @@ def test_python_constants_match_header():
         "ACT_NONE": _lib.ACT_NONE, "ACT_RELU": _lib.ACT_RELU, "ACT_GELU": _lib.ACT_GELU,
         "ACT_GELU_TANH": _lib.ACT_GELU_TANH, "ACT_SILU": _lib.ACT_SILU,
         "OUT_BF16": _lib.OUT_BF16, "OUT_F32": _lib.OUT_F32, "OUT_E4M3": _lib.OUT_E4M3,
+        "PDL_OFF": _lib.PDL_OFF, "PDL_ON": _lib.PDL_ON, "PDL_WEIGHTS_EARLY": _lib.PDL_WEIGHTS_EARLY,
     }
     for name, value in mirror.items():
         assert defines.get(name) == value, name
