@@ -208,11 +208,11 @@ class Gemm:
         _lib.check(self._lib.b200gemm_set_small_m(self._h, int(mode)), "b200gemm_set_small_m")
 
     def set_pdl(self, mode: int) -> None:
-        """Launch overlap of the small-M kernels with the previous kernel on
-        the stream: _lib.PDL_OFF (default), PDL_ON (setup overlaps; every
-        global access waits for the previous kernel) or PDL_WEIGHTS_EARLY (B
-        also starts streaming before that wait; the previous kernel must not
-        write B)."""
+        """Launch overlap with the previous kernel on the stream:
+        _lib.PDL_OFF (default), PDL_ON (setup overlaps; every global access
+        waits for the previous kernel) or PDL_WEIGHTS_EARLY (the small-M
+        kernels also start streaming B before that wait, so the previous
+        kernel must not write B; the tiled kernel treats it as PDL_ON)."""
         _lib.check(self._lib.b200gemm_set_pdl(self._h, int(mode)), "b200gemm_set_pdl")
 
     def small_m_split(self, M: int, N: int, K: int) -> int:

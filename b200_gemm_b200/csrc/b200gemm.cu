@@ -310,6 +310,13 @@ cudaError_t launch_gemm(int clusters, cudaStream_t stream, const CUtensorMap& ma
   cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
   cfg.dynamicSmemBytes = Cfg::kSmemBytes;
   cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  if (p.pdl != kPdlOff) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
   return cudaLaunchKernelEx(&cfg, gemm_bf16_nt_sm100<Cfg>, ma, mb, mc, p);
 }
 
@@ -1046,6 +1053,9 @@ int gemm_device(b200gemm_t h, int M, int N, int K, const void* A, const void* B,
   p.npeers = npeers;
   for (int i = 0; i < GemmParams::kMaxPeers; ++i)
     p.peer_c[i] = i < npeers ? static_cast<uint8_t*>(peers[i]) : nullptr;
+  // Launch overlap (no B-first variant here: the tile table comes first);
+  // the all-gather form keeps plain stream order.
+  p.pdl = (pdl != kPdlOff && npeers == 0) ? kPdlOn : kPdlOff;
 
   p.epi_flags = 0;
   p.act = B200GEMM_ACT_NONE;

@@ -110,6 +110,7 @@ struct GemmParams {
   const uint16_t* bias;        // bf16[N]
   const uint16_t* residual;    // bf16, row pitch ldr elements
   long long ldr;
+  int pdl;                     // kPdlOff or kPdlOn (launch overlap with the previous kernel)
 };
 
 constexpr uint32_t kEpiBias = 1u;
@@ -607,6 +608,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
   ptx::tc_fence_after();
   uint32_t tmem_base;
   asm volatile("ld.shared.u32 %0, [%1];" : "=r"(tmem_base) : "r"(tmem_slot) : "memory");
+  // Launched to overlap the previous kernel (kPdlOn), the setup above ran
+  // during its tail; the tile table, A, B, C and the epilogue operands may
+  // all be its output, so nothing global is touched before it completes.
+  ptx::griddep_wait();
 
   const uint32_t num_units = static_cast<uint32_t>(p.num_units);
 
@@ -647,6 +652,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
       }
     }
     __syncwarp();
+    if (p.pdl != kPdlOff) ptx::griddep_launch_dependents();
   } else if (warp == 1) {
     // ----------------------------------------------------------------- MMA
     if (leader && lane == 0) {
@@ -701,6 +707,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
       ptx::mbar_wait_drain(drain, 0, dwd, kSiteDrain);
     }
     __syncwarp();
+    if (p.pdl != kPdlOff) ptx::griddep_launch_dependents();
   } else {
     // ------------------------------------------------------------ epilogue
     const uint32_t e = warp - 2u;         // epilogue warp index
@@ -739,6 +746,8 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
       const bool full_ok = ptx::mbar_wait(tfull0 + 8 * acc, acc_phase, wd, kSiteEpilogue, t);
       const bool live = __all_sync(0xFFFFFFFFu, full_ok);  // warp-uniform
       ptx::tc_fence_after();
+      // The last accumulator is complete: the next kernel may start its setup.
+      if (p.pdl != kPdlOff && t + nclusters >= num_units) ptx::griddep_launch_dependents();
       const uint32_t t_row =
           tmem_base + ((quarter * 32u) << 16) + acc * Cfg::kAccStride + nblk * Cfg::kColsPerWarp;
       if (cur.slot < 0 && !live) {

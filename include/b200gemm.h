@@ -201,7 +201,7 @@ int b200gemm_tile_width_for(b200gemm_t handle, int M, int N, int K);
  * 0: always use the tiled kernel.  The reference has no small-M path. */
 int b200gemm_set_small_m(b200gemm_t handle, int mode);
 
-/* Launch overlap for the small-M kernels (programmatic dependent launch).
+/* Launch overlap with the previous kernel (programmatic dependent launch).
  * OFF (default): a call starts after the previous work on the stream.
  * ON: the kernel may be scheduled while the previous kernel on the stream is
  *   still running; it sets up (barriers, tensor memory) and then waits for
@@ -210,9 +210,11 @@ int b200gemm_set_small_m(b200gemm_t handle, int mode);
  * WEIGHTS_EARLY: as ON, and the first ring of B (the weights) is requested
  *   before that wait, so streaming B overlaps the previous kernel's tail.
  *   The caller guarantees that the previous kernel does not write B.
- * Other kernels and work on the stream (copies, events) are unaffected, and
- * the tiled kernel always launches without overlap.  The reference launches
- * one kernel per call with no overlap (matmul_1.cuh:416). */
+ * The tiled kernel (M > 128) takes WEIGHTS_EARLY as ON: it reads its tile
+ * table before any operand.  The multi-GPU all-gather form never overlaps.
+ * Work on the stream other than these kernels (copies, events, other
+ * kernels) keeps plain stream order.  The reference launches one kernel per
+ * call with no overlap (matmul_1.cuh:416). */
 #define B200GEMM_PDL_OFF 0
 #define B200GEMM_PDL_ON 1
 #define B200GEMM_PDL_WEIGHTS_EARLY 2

@@ -1,4 +1,4 @@
-"""Programmatic dependent launch of the small-M kernels (b200gemm_set_pdl).
+"""Programmatic dependent launch (b200gemm_set_pdl): small-M and tiled kernels.
 
 A chain of decode-shaped GEMMs where every call reads the previous call's
 output: X[i+1] = gelu_tanh(X[i] . W[i]^T + bias) + X[i] (the residual is the
@@ -15,15 +15,18 @@ pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
 
 MODES = [_lib.PDL_ON, _lib.PDL_WEIGHTS_EARLY]
-# (M, K = N, plan kernel): the pair kernel and the single-CTA kernel
-CHAINS = [(128, 8192, "small_m"), (96, 4096, "small_m_1cta")]
+# (M, K = N, plan kernel): the pair kernel, the single-CTA kernel, the tiled kernel
+CHAINS = [(128, 8192, "small_m"), (96, 4096, "small_m_1cta"), (512, 4096, "tiled")]
 STEPS = 6
 
 
-def _chain(h, X0, Ws, bias, outs):
+def _chain(h, X0, Ws, bias, outs, fused=True):
     x = X0
     for W, out in zip(Ws, outs):
-        h.bf16_nt_epilogue(x, W, bias=bias, activation="gelu_tanh", residual=x, out=out)
+        if fused:
+            h.bf16_nt_epilogue(x, W, bias=bias, activation="gelu_tanh", residual=x, out=out)
+        else:
+            h.bf16_nt(x, W, out=out)
         x = out
     return outs
 
@@ -41,18 +44,19 @@ def chain_operands():
 
 @pytest.mark.parametrize("M,K,kernel", CHAINS)
 @pytest.mark.parametrize("mode", MODES, ids=["on", "weights_early"])
-def test_dependent_chain_matches_serial(gpu_handle, chain_operands, M, K, kernel, mode):
+@pytest.mark.parametrize("fused", [True, False], ids=["bias_gelu_residual", "plain"])
+def test_dependent_chain_matches_serial(gpu_handle, chain_operands, M, K, kernel, mode, fused):
     h = gpu_handle
     assert h.plan(M, K, K)["kernel"] == kernel
     X0, Ws, bias = chain_operands(M, K)
     ref = [torch.empty(M, K, dtype=torch.bfloat16, device="cuda") for _ in range(STEPS)]
-    _chain(h, X0, Ws, bias, ref)
+    _chain(h, X0, Ws, bias, ref, fused)
     torch.cuda.synchronize()
     h.set_pdl(mode)
     try:
         for _ in range(3):
             outs = [torch.full((M, K), float("nan"), dtype=torch.bfloat16, device="cuda") for _ in range(STEPS)]
-            _chain(h, X0, Ws, bias, outs)
+            _chain(h, X0, Ws, bias, outs, fused)
             torch.cuda.synchronize()
             for r, o in zip(ref, outs):
                 assert torch.equal(r.view(torch.int16), o.view(torch.int16))
@@ -62,9 +66,10 @@ def test_dependent_chain_matches_serial(gpu_handle, chain_operands, M, K, kernel
 
 
 @pytest.mark.parametrize("mode", MODES, ids=["on", "weights_early"])
-def test_dependent_chain_in_cuda_graph(gpu_handle, chain_operands, mode):
+@pytest.mark.parametrize("chain", [0, 2], ids=["small_m", "tiled"])
+def test_dependent_chain_in_cuda_graph(gpu_handle, chain_operands, mode, chain):
     h = gpu_handle
-    M, K, _ = CHAINS[0]
+    M, K, _ = CHAINS[chain]
     X0, Ws, bias = chain_operands(M, K)
     ref = [torch.empty(M, K, dtype=torch.bfloat16, device="cuda") for _ in range(STEPS)]
     _chain(h, X0, Ws, bias, ref)
