@@ -856,6 +856,7 @@ int run_decode(b200gemm_t h, int split, int M, int N, int K, const void* A, cons
   p.K = K;
   p.num_kb = (K + kBlockK - 1) / kBlockK;
   p.kb_per_split = (p.num_kb + split - 1) / split;
+  p.kb_per_split = (p.kb_per_split + kDecodeKps - 1) / kDecodeKps * kDecodeKps;  // whole stages per pair
   p.status = h->status_dev;
   p.timeout_ns = timeout_ns;
   p.pdl = pdl;

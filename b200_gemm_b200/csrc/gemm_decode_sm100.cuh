@@ -31,10 +31,12 @@
 
 namespace b200gemm {
 
+constexpr int kDecodeKps = 2;  // K blocks per pipeline stage of the pair kernel
+
 struct DecodeParams {
   int M, N, K;
   int num_kb;        // ceil(K / 64)
-  int kb_per_split;  // K blocks per CTA pair
+  int kb_per_split;  // K blocks per CTA pair, a multiple of kDecodeKps
   unsigned int* status;
   unsigned long long timeout_ns;
   EpiArgs epi;       // fused epilogue (identity: no flags, act none, bf16, alpha 1)
@@ -48,8 +50,14 @@ struct DecodeCfg {
   static constexpr int kNT = 128;                  // rows of A covered (MMA N)
   static constexpr int kClusterSize = 2 * S;
   static constexpr int kThreads = 192;             // warps: 0 TMA, 1 MMA, 2-5 epilogue
-  static constexpr int kStageB = 128 * kBlockK * 2;          // 16 KB: this CTA's 128 rows of B
-  static constexpr int kStageA = (kNT / 2) * kBlockK * 2;     // 8 KB: this CTA's 64 rows of A
+  // A stage holds kKps consecutive K blocks, requested back to back, so each
+  // row of B is read 256 contiguous bytes at a time (measured: equal or up to
+  // 9% faster than one K block per stage, most where few SMs stream).
+  static constexpr int kKps = kDecodeKps;
+  static constexpr int kSubB = 128 * kBlockK * 2;             // 16 KB: this CTA's 128 rows of B, one K block
+  static constexpr int kSubA = (kNT / 2) * kBlockK * 2;       // 8 KB: this CTA's 64 rows of A, one K block
+  static constexpr int kStageB = kKps * kSubB;
+  static constexpr int kStageA = kKps * kSubA;
   static constexpr int kStageBytes = kStageB + kStageA;
   static constexpr int kSliceRows = kNT / S;                 // rows of C each CTA finishes
   static constexpr int kRecvSlotBytes = 128 * kSliceRows * 4;  // [kSliceRows/4][128 rows][4] fp32
@@ -60,7 +68,7 @@ struct DecodeCfg {
   // The ring takes every byte left: its depth is what hides HBM latency.
   static constexpr int kStagesFit = (232448 - 1024 - kBarBytes - kRecvBytes) / kStageBytes;
   static constexpr int kStages = kStagesFit > 10 ? 10 : kStagesFit;
-  static_assert(kStages >= 4, "pipeline too shallow");
+  static_assert(kStages >= 3, "pipeline too shallow");
   static_assert(4 * (kCWarpBytes + kRWarpBytes) <= kStages * kStageB, "C staging and residual tiles alias the B stages");
   static constexpr int kB = 0;       // B stages; after the last MMA they hold the C staging buffers
   static constexpr int kA = kB + kStages * kStageB;
@@ -154,27 +162,40 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       // With kPdlWeightsEarly the first ring of B (the weights, which the
       // previous kernel does not write) streams in before that kernel has
       // finished; A and everything after wait for it.
-      const int pre = p.pdl == kPdlWeightsEarly ? min(STAGES, nkb) : 0;
+      // Each stage covers K blocks [kb, kb + KPS); the pair's range is a whole
+      // number of stages (a block past K reads as zeros).
+      constexpr int KPS = Cfg::kKps;
+      const int brow = n0 + static_cast<int>(half) * 128, arow = static_cast<int>(half) * (Cfg::kNT / 2);
+      const int nst = (nkb + KPS - 1) / KPS;
+      const int pre = p.pdl == kPdlWeightsEarly ? min(STAGES, nst) : 0;
       for (int s = 0; s < pre; ++s) {
         if (leader) ptx::mbar_arrive_expect_tx(full0 + 8 * s, 2 * Cfg::kStageBytes);
-        ptx::tma_load_2d_cg2(sB + s * Cfg::kStageB, &map_b, full_leader0 + 8 * s, (kb_begin + s) * kBlockK,
-                             n0 + static_cast<int>(half) * 128, policy_b);
+#pragma unroll
+        for (int j = 0; j < KPS; ++j)
+          ptx::tma_load_2d_cg2(sB + s * Cfg::kStageB + j * Cfg::kSubB, &map_b, full_leader0 + 8 * s,
+                               (kb_begin + s * KPS + j) * kBlockK, brow, policy_b);
       }
       ptx::griddep_wait();
       for (int s = 0; s < pre; ++s) {
-        ptx::tma_load_2d_cg2(sA + s * Cfg::kStageA, &map_a, full_leader0 + 8 * s, (kb_begin + s) * kBlockK,
-                             static_cast<int>(half) * (Cfg::kNT / 2), policy_a);
+#pragma unroll
+        for (int j = 0; j < KPS; ++j)
+          ptx::tma_load_2d_cg2(sA + s * Cfg::kStageA + j * Cfg::kSubA, &map_a, full_leader0 + 8 * s,
+                               (kb_begin + s * KPS + j) * kBlockK, arow, policy_a);
       }
       uint32_t stage = pre == STAGES ? 0u : static_cast<uint32_t>(pre);
       uint32_t phase = pre == STAGES ? 1u : 0u;
-      for (int kb = kb_begin + pre; kb < kb_end; ++kb) {
+      for (int kb = kb_begin + pre * KPS; kb < kb_end; kb += KPS) {
         if (!ptx::mbar_wait(empty0 + 8 * stage, phase ^ 1u, wd, kSiteProducer, 0)) break;
         if (leader) ptx::mbar_arrive_expect_tx(full0 + 8 * stage, 2 * Cfg::kStageBytes);
         const uint32_t fb = full_leader0 + 8 * stage;
-        ptx::tma_load_2d_cg2(sB + stage * Cfg::kStageB, &map_b, fb, kb * kBlockK,
-                             n0 + static_cast<int>(half) * 128, policy_b);
-        ptx::tma_load_2d_cg2(sA + stage * Cfg::kStageA, &map_a, fb, kb * kBlockK,
-                             static_cast<int>(half) * (Cfg::kNT / 2), policy_a);
+#pragma unroll
+        for (int j = 0; j < KPS; ++j)
+          ptx::tma_load_2d_cg2(sB + stage * Cfg::kStageB + j * Cfg::kSubB, &map_b, fb, (kb + j) * kBlockK, brow,
+                               policy_b);
+#pragma unroll
+        for (int j = 0; j < KPS; ++j)
+          ptx::tma_load_2d_cg2(sA + stage * Cfg::kStageA + j * Cfg::kSubA, &map_a, fb, (kb + j) * kBlockK, arow,
+                               policy_a);
         if (++stage == STAGES) {
           stage = 0;
           phase ^= 1u;
@@ -189,18 +210,21 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       const uint32_t own_empty0 = ptx::mapa(empty0, rank), peer_empty0 = ptx::mapa(empty0, rank + 1);
       uint32_t stage = 0, phase = 0;
       bool ok = true;
-      for (int kb = kb_begin; kb < kb_end; ++kb) {
+      for (int kb = kb_begin; kb < kb_end; kb += Cfg::kKps) {
         if (!ptx::mbar_wait(full0 + 8 * stage, phase, wd, kSiteMmaFull, 0)) {
           ok = false;
           break;
         }
         ptx::tc_fence_after();
-        const uint64_t a_desc = smem_desc(sB + stage * Cfg::kStageB);  // MMA A operand: rows of B
-        const uint64_t b_desc = smem_desc(sA + stage * Cfg::kStageA);  // MMA B operand: rows of A
 #pragma unroll
-        for (int k = 0; k < kBlockK / kMmaK; ++k) {
-          ptx::mma_bf16_cg2(tmem_base, a_desc + 2 * k, b_desc + 2 * k, kIdescDecode,
-                            (kb > kb_begin || k > 0) ? 1u : 0u);
+        for (int j = 0; j < Cfg::kKps; ++j) {
+          const uint64_t a_desc = smem_desc(sB + stage * Cfg::kStageB + j * Cfg::kSubB);  // MMA A: rows of B
+          const uint64_t b_desc = smem_desc(sA + stage * Cfg::kStageA + j * Cfg::kSubA);  // MMA B: rows of A
+#pragma unroll
+          for (int k = 0; k < kBlockK / kMmaK; ++k) {
+            ptx::mma_bf16_cg2(tmem_base, a_desc + 2 * k, b_desc + 2 * k, kIdescDecode,
+                              (kb > kb_begin || j > 0 || k > 0) ? 1u : 0u);
+          }
         }
         ptx::mma_commit_cg2(own_empty0 + 8 * stage);
         ptx::mma_commit_cg2(peer_empty0 + 8 * stage);

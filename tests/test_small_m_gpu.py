@@ -36,6 +36,8 @@ CASES = [
     (77, 2048, 1000, "small_m", 4),     # ragged M and K
     (128, 2048, 576, "small_m", 4),     # 9 K blocks over 4 pairs: the last pair has none
     (100, 1032, 384, "small_m", 2),     # N not a multiple of 256: the last cluster is ragged
+    (128, 8192, 8128, "small_m", 2),    # 127 K blocks: the last stage's second block lies past K
+    (64, 16384, 320, "small_m", 1),     # 5 K blocks in stages of 2
 ]
 
 
