@@ -1079,11 +1079,12 @@ int gemm_device(b200gemm_t h, int M, int N, int K, const void* A, const void* B,
   }
 
   const int max_clusters = fused ? h->clusters_epi[width_index(width)] : h->clusters_w[width_index(width)];
-  const int clusters = p.num_tiles < max_clusters ? p.num_tiles : max_clusters;
+  int clusters = p.num_tiles < max_clusters ? p.num_tiles : max_clusters;
   // Split the last partial wave along K when it leaves clusters idle (plain
-  // epilogue only: the split tiles' reduction writes bf16 directly).
+  // epilogue only: the split tiles' reduction writes bf16 directly).  With
+  // fewer tiles than clusters the one wave is all tail: every tile is split.
   const int sk = (tail_split_enabled_for(h) && tail_split_width(width, fused))
-                     ? tail_split_for(p.num_tiles, clusters, p.num_kb)
+                     ? tail_split_for(p.num_tiles, max_clusters, p.num_kb)
                      : 1;
   p.tail_start = p.num_tiles;
   p.tail_split = 1;
@@ -1093,7 +1094,7 @@ int gemm_device(b200gemm_t h, int M, int N, int K, const void* A, const void* B,
   p.tail_counters = nullptr;
   bool tail_on = false;
   if (sk >= 2) {
-    const int rem = p.num_tiles % clusters;
+    const int rem = p.num_tiles % max_clusters;
     const size_t need = static_cast<size_t>(rem) * sk * 2 * 128 * width * sizeof(float);
     std::lock_guard<std::mutex> lock(h->mu);
     bool have_ws = h->tail_ws_bytes >= need;
@@ -1111,6 +1112,7 @@ int gemm_device(b200gemm_t h, int M, int N, int K, const void* A, const void* B,
       p.tail_split = sk;
       p.tail_kb = (p.num_kb + sk - 1) / sk;
       p.num_units = p.tail_start + rem * sk;
+      clusters = p.num_units < max_clusters ? p.num_units : max_clusters;
       p.workspace = h->tail_ws;
       p.tail_counters = h->tail_counters;
       tail_on = true;
@@ -1146,13 +1148,15 @@ extern "C" int b200gemm_plan(b200gemm_t h, int M, int N, int K, int* plan) {
   const int width = choose_tile_width(h, M, N, K);
   const int tiles = ((M + kTileM - 1) / kTileM) * ((N + width - 1) / width);
   const int maxc = h->clusters_w[width_index(width)];
-  const int clusters = tiles < maxc ? tiles : maxc;
   const int num_kb = (K + kBlockK - 1) / kBlockK;
+  const int sk = (h->tail_split_enabled && tail_split_width(width, false)) ? tail_split_for(tiles, maxc, num_kb) : 1;
+  const int units = tiles + (sk >= 2 ? (tiles % maxc) * (sk - 1) : 0);
+  const int clusters = units < maxc ? units : maxc;
   plan[0] = 1;  // tiled kernel
   plan[1] = width;
   plan[2] = tiles;
   plan[3] = clusters;
-  plan[4] = (h->tail_split_enabled && tail_split_width(width, false)) ? tail_split_for(tiles, clusters, num_kb) : 1;
+  plan[4] = sk;
   return B200GEMM_OK;
 }
 

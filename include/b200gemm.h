@@ -177,7 +177,8 @@ int b200gemm_set_tile_width(b200gemm_t handle, int width);
 
 /* Split the last, partial wave of tiles along K (default off): when T tiles
  * leave the last wave of G clusters partly idle, each of its T mod G tiles is
- * cut into up to 6 K slices run on the idle clusters; the slices write fp32
+ * cut into up to 6 K slices run on the idle clusters (with T < G the single
+ * wave is all tail and every tile is split); the slices write fp32
  * partials to a workspace owned by the handle and the last one to finish
  * adds them and writes C.  Split launches on one handle are serialised with
  * an event (they share the workspace).  No reference counterpart. */
