@@ -417,6 +417,7 @@ struct b200gemm_handle {
   int clusters_w[kNumWidths] = {};  // co-resident clusters of each width's instance
   int clusters_epi[kNumWidths] = {};  // the same for the fused-epilogue instances
   int decode_clusters[5] = {};        // [S]: co-resident clusters of the small-M pair kernel, split S
+  int decode256_clusters[5] = {};     // the same for its instances covering 256 rows of A
   int smallm1_clusters[5] = {};       // [S]: the same for the single-CTA small-M kernel
   int tile_width = 0;         // 0 = choose per call, else one of kWidths
   int small_m = -1;           // small-M kernel: -1 or 1 = use it when eligible, 0 = never
@@ -484,6 +485,9 @@ extern "C" int b200gemm_create(b200gemm_t* out, int device) {
   const int dc1 = prepare_decode_kernel<DecodeCfg<1>>(sms), dc2 = prepare_decode_kernel<DecodeCfg<2>>(sms),
             dc4 = prepare_decode_kernel<DecodeCfg<4>>(sms);
   if (dc1 <= 0 || dc2 <= 0 || dc4 <= 0) return B200GEMM_ERR_CUDA;
+  const int dw1 = prepare_decode_kernel<DecodeCfg<1, 256>>(sms), dw2 = prepare_decode_kernel<DecodeCfg<2, 256>>(sms),
+            dw4 = prepare_decode_kernel<DecodeCfg<4, 256>>(sms);
+  if (dw1 <= 0 || dw2 <= 0 || dw4 <= 0) return B200GEMM_ERR_CUDA;
   const int sc2 = prepare_smallm1_kernel<SmallMCfg<2>>(sms), sc4 = prepare_smallm1_kernel<SmallMCfg<4>>(sms);
   if (sc2 <= 0 || sc4 <= 0) return B200GEMM_ERR_CUDA;
 
@@ -493,6 +497,9 @@ extern "C" int b200gemm_create(b200gemm_t* out, int device) {
   h->decode_clusters[1] = dc1;
   h->decode_clusters[2] = dc2;
   h->decode_clusters[4] = dc4;
+  h->decode256_clusters[1] = dw1;
+  h->decode256_clusters[2] = dw2;
+  h->decode256_clusters[4] = dw4;
   h->smallm1_clusters[2] = sc2;
   h->smallm1_clusters[4] = sc4;
   h->max_clusters = cw[0];
@@ -716,17 +723,19 @@ cudaError_t launch_width(int width, bool fused, int clusters, cudaStream_t strea
 namespace {
 
 // K split for the small-M kernel, or 0 when the tiled kernel should run:
-// M <= 128, N % 8 == 0 (its C stores are whole 16-byte groups), and the
+// M <= 256, N % 8 == 0 (its C stores are whole 16-byte groups), and the
 // largest S in {4, 2} whose N / 256 clusters of 2S CTAs are all co-resident
-// (decode_clusters[S], from the occupancy query: a cluster must fit in one
-// GPC, so fewer than sm_count / 2S fit, and a second wave would double the
-// time) while every CTA pair keeps at least two K blocks, else 1.
+// (decode_clusters[S] for M <= 128, decode256_clusters[S] above, from the
+// occupancy query: a cluster must fit in one GPC, so fewer than sm_count / 2S
+// fit, and a second wave would double the time) while every CTA pair keeps
+// at least two K blocks, else 1.
 int decode_split(const b200gemm_handle* h, int M, int N, int K) {
-  if (M > 128 || (N % 8) != 0 || K < 2 * kBlockK) return 0;
+  if (M > 256 || (N % 8) != 0 || K < 2 * kBlockK) return 0;
   const int clusters = (N + 255) / 256;
   const int num_kb = (K + kBlockK - 1) / kBlockK;
+  const int* fit = M > 128 ? h->decode256_clusters : h->decode_clusters;
   for (int s : {4, 2}) {
-    if (clusters <= h->decode_clusters[s] && num_kb >= 2 * s) return s;
+    if (clusters <= fit[s] && num_kb >= 2 * s) return s;
   }
   return 1;
 }
@@ -793,6 +802,7 @@ bool encode_smallm_c(CUtensorMap* mc, void* C, int M, int N, int ldc, uint32_t s
 SmallMPlan smallm_plan(const b200gemm_handle* h, int M, int N, int K) {
   const int sp = decode_split(h, M, N, K);
   if (sp == 0) return {0, 0};
+  if (M > 128) return {2, sp};  // the single-CTA kernel covers at most 128 rows of A
   const int ctas_pair = (N + 255) / 256 * 2 * sp;
   const int clusters1 = (N + 127) / 128;
   const int num_kb = (K + kBlockK - 1) / kBlockK;
@@ -841,9 +851,10 @@ int run_decode(b200gemm_t h, int split, int M, int N, int K, const void* A, cons
                const b200gemm_epilogue* epi) {
   const uint64_t k = static_cast<uint64_t>(K);
   CUtensorMap ma, mb, mc, mr;
-  const uint32_t slice_rows = static_cast<uint32_t>(128 / split);
+  const int nt = M > 128 ? 256 : 128;  // rows of A one MMA covers
+  const uint32_t slice_rows = static_cast<uint32_t>(nt / split);
   const EpiArgs ea = epi_args(epi);
-  if (!encode_2d(&ma, A, k, static_cast<uint64_t>(M), k * 2, kBlockK, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
+  if (!encode_2d(&ma, A, k, static_cast<uint64_t>(M), k * 2, kBlockK, nt / 2, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !encode_2d(&mb, B, k, static_cast<uint64_t>(N), k * 2, kBlockK, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !encode_smallm_c(&mc, C, M, N, ldc, slice_rows, ea.out_type) ||
       !encode_smallm_r(&mr, mc, epi, M, N, slice_rows)) {
@@ -856,14 +867,21 @@ int run_decode(b200gemm_t h, int split, int M, int N, int K, const void* A, cons
   p.K = K;
   p.num_kb = (K + kBlockK - 1) / kBlockK;
   p.kb_per_split = (p.num_kb + split - 1) / split;
-  p.kb_per_split = (p.kb_per_split + kDecodeKps - 1) / kDecodeKps * kDecodeKps;  // whole stages per pair
+  const int kps = nt == 256 ? DecodeCfg<1, 256>::kKps : DecodeCfg<1, 128>::kKps;
+  p.kb_per_split = (p.kb_per_split + kps - 1) / kps * kps;  // whole stages per pair
   p.status = h->status_dev;
   p.timeout_ns = timeout_ns;
   p.pdl = pdl;
   cudaError_t e;
-  if (split == 4) e = launch_decode<DecodeCfg<4>>(stream, ma, mb, mc, mr, p);
-  else if (split == 2) e = launch_decode<DecodeCfg<2>>(stream, ma, mb, mc, mr, p);
-  else e = launch_decode<DecodeCfg<1>>(stream, ma, mb, mc, mr, p);
+  if (nt == 256) {
+    if (split == 4) e = launch_decode<DecodeCfg<4, 256>>(stream, ma, mb, mc, mr, p);
+    else if (split == 2) e = launch_decode<DecodeCfg<2, 256>>(stream, ma, mb, mc, mr, p);
+    else e = launch_decode<DecodeCfg<1, 256>>(stream, ma, mb, mc, mr, p);
+  } else {
+    if (split == 4) e = launch_decode<DecodeCfg<4>>(stream, ma, mb, mc, mr, p);
+    else if (split == 2) e = launch_decode<DecodeCfg<2>>(stream, ma, mb, mc, mr, p);
+    else e = launch_decode<DecodeCfg<1>>(stream, ma, mb, mc, mr, p);
+  }
   return e == cudaSuccess ? B200GEMM_OK : B200GEMM_ERR_CUDA;
 }
 
@@ -1352,7 +1370,7 @@ extern "C" int b200gemm_bf16_nt_host(b200gemm_t h, int M, int N, int K, const vo
         !ok(cudaStreamWaitEvent(st.s_mma, st.ev_a[i], 0)))
       return B200GEMM_ERR_CUDA;
     const int rc = gemm_device(h, rows, N, K, dA + a_off, buf.dB, dC + r0 * ldc_dev * 2,
-                               static_cast<int>(ldc_dev), st.s_mma, /*allow_small_m=*/M <= 128);
+                               static_cast<int>(ldc_dev), st.s_mma, /*allow_small_m=*/M <= 256);
     if (rc != B200GEMM_OK) return rc;
     if (!ok(cudaEventRecord(st.ev_c[i], st.s_mma)) ||
         !ok(cudaStreamWaitEvent(st.s_d2h, st.ev_c[i], 0)) ||

@@ -1,11 +1,11 @@
 // Small-M ("decode") GEMM for sm_100a: C[M x N] = A[M x K] . B[N x K]^T with
-// M <= 128, where streaming B from HBM is the whole cost (at M = 128,
+// M <= 256, where streaming B from HBM is the whole cost (at M = 128,
 // N = K = 8192, B is 128 MB and A is 2 MB).
 //
 // The tiled kernel (gemm_sm100.cuh) gives a CTA pair 256 rows of C, so at
 // M = 128 half of every MMA is padding and only N / 256 pairs (32 of 74 at
 // N = 8192) have work.  Here the operands swap roles: rows of B are the MMA's
-// M side and the (at most 128) rows of A its N side, so a pair covers 256
+// M side and the (at most 128, or 256) rows of A its N side, so a pair covers 256
 // rows of B against all of A, and K is split across the S pairs of a
 // cluster of 2S CTAs.  Each CTA pair accumulates its K range in TMEM
 // (D[i][j] = sum_k B[n0 + i][k] * A[j][k] = C[j][n0 + i]); the pairs then
@@ -14,7 +14,7 @@
 // [column group of 4][B row][4 floats], so the 32 lanes of a warp, which hold
 // 32 consecutive B rows, write 512 contiguous bytes per store and read them
 // back bank-conflict free): CTA (pair p, half q) keeps the slice of
-// A rows j in [p * 128/S, (p+1) * 128/S), receives the other pairs' partials
+// A rows j in [p * NT/S, (p+1) * NT/S), receives the other pairs' partials
 // of that slice, adds them, rounds to bf16 and writes C through a transposing
 // staging buffer.  No global workspace, one launch, N/256 * 2S CTAs.
 //
@@ -31,31 +31,34 @@
 
 namespace b200gemm {
 
-constexpr int kDecodeKps = 2;  // K blocks per pipeline stage of the pair kernel
 
 struct DecodeParams {
   int M, N, K;
   int num_kb;        // ceil(K / 64)
-  int kb_per_split;  // K blocks per CTA pair, a multiple of kDecodeKps
+  int kb_per_split;  // K blocks per CTA pair, a multiple of the instance's kKps
   unsigned int* status;
   unsigned long long timeout_ns;
   EpiArgs epi;       // fused epilogue (identity: no flags, act none, bf16, alpha 1)
   int pdl;           // launch overlap with the previous kernel: kPdl*
 };
 
-template <int S>
+// NT = rows of A covered (the MMA's N): 128 for M <= 128, 256 for M <= 256.
+template <int S, int NT = 128>
 struct DecodeCfg {
   static_assert(S == 1 || S == 2 || S == 4, "split factor");
+  static_assert(NT == 128 || NT == 256, "rows of A per MMA");
   static constexpr int kSplit = S;
-  static constexpr int kNT = 128;                  // rows of A covered (MMA N)
+  static constexpr int kNT = NT;
   static constexpr int kClusterSize = 2 * S;
   static constexpr int kThreads = 192;             // warps: 0 TMA, 1 MMA, 2-5 epilogue
-  // A stage holds kKps consecutive K blocks, requested back to back, so each
-  // row of B is read 256 contiguous bytes at a time (measured: equal or up to
-  // 9% faster than one K block per stage, most where few SMs stream).
-  static constexpr int kKps = kDecodeKps;
+  // With NT = 128 a stage holds 2 consecutive K blocks, requested back to
+  // back, so each row of B is read 256 contiguous bytes at a time (measured:
+  // equal or up to 9% faster than one K block per stage, most where few SMs
+  // stream).  NT = 256 doubles A's share and its partial sums, leaving room
+  // for one K block per stage.
+  static constexpr int kKps = NT == 128 ? 2 : 1;
   static constexpr int kSubB = 128 * kBlockK * 2;             // 16 KB: this CTA's 128 rows of B, one K block
-  static constexpr int kSubA = (kNT / 2) * kBlockK * 2;       // 8 KB: this CTA's 64 rows of A, one K block
+  static constexpr int kSubA = (kNT / 2) * kBlockK * 2;       // this CTA's NT/2 rows of A, one K block
   static constexpr int kStageB = kKps * kSubB;
   static constexpr int kStageA = kKps * kSubA;
   static constexpr int kStageBytes = kStageB + kStageA;
@@ -69,8 +72,11 @@ struct DecodeCfg {
   static constexpr int kStagesFit = (232448 - 1024 - kBarBytes - kRecvBytes) / kStageBytes;
   static constexpr int kStages = kStagesFit > 10 ? 10 : kStagesFit;
   static_assert(kStages >= 3, "pipeline too shallow");
-  static_assert(4 * (kCWarpBytes + kRWarpBytes) <= kStages * kStageB, "C staging and residual tiles alias the B stages");
-  static constexpr int kB = 0;       // B stages; after the last MMA they hold the C staging buffers
+  static_assert(4 * (kCWarpBytes + kRWarpBytes) <= kStages * kStageBytes,
+                "C staging and residual tiles alias the operand ring");
+  static constexpr int kB = 0;       // B stages, then A stages; after the last MMA the ring holds C staging
+  static constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((static_cast<uint32_t>(NT) >> 3) << 17) |
+                                     ((256u >> 4) << 24);
   static constexpr int kA = kB + kStages * kStageB;
   static constexpr int kRecv = kA + kStages * kStageA;
   static constexpr int kFull = kRecv + kRecvBytes;
@@ -87,9 +93,8 @@ struct DecodeCfg {
   static_assert(kSmemBytes <= 232448, "exceeds the 227 KB per-CTA shared memory limit");
 };
 
-// kind::f16, D f32, A = B = bf16 K-major, M = 256 (pair), N = 128.
-constexpr uint32_t kIdescDecode = (1u << 4) | (1u << 7) | (1u << 10) | ((128u >> 3) << 17) |
-                                  ((256u >> 4) << 24);
+// Instruction descriptor (DecodeCfg::kIdesc): kind::f16, D f32, A = B =
+// bf16 K-major, M = 256 (pair), N = NT.
 
 template <class Cfg>
 __global__ void __launch_bounds__(Cfg::kThreads, 1)
@@ -113,7 +118,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
   const int nkb = kb_end > kb_begin ? kb_end - kb_begin : 0;
 
   const uint32_t sB = base + Cfg::kB, sA = base + Cfg::kA, sRecv = base + Cfg::kRecv;
-  const uint32_t sC = sB;  // C staging reuses the B stages once the MMAs are done
+  const uint32_t sC = sB;  // C staging reuses the operand ring once the MMAs are done
   const uint32_t full0 = base + Cfg::kFull, empty0 = base + Cfg::kEmpty;
   const uint32_t tfull = base + Cfg::kTFull, recv_bar = base + Cfg::kRecvBar;
   const uint32_t drain = base + Cfg::kDrain, tmem_slot = base + Cfg::kTmemSlot;
@@ -222,7 +227,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
           const uint64_t b_desc = smem_desc(sA + stage * Cfg::kStageA + j * Cfg::kSubA);  // MMA B: rows of A
 #pragma unroll
           for (int k = 0; k < kBlockK / kMmaK; ++k) {
-            ptx::mma_bf16_cg2(tmem_base, a_desc + 2 * k, b_desc + 2 * k, kIdescDecode,
+            ptx::mma_bf16_cg2(tmem_base, a_desc + 2 * k, b_desc + 2 * k, Cfg::kIdesc,
                               (kb > kb_begin || j > 0 || k > 0) ? 1u : 0u);
           }
         }

@@ -84,12 +84,12 @@ typedef struct b200gemm_epilogue {
 
 /* C = epilogue(A . B^T) with the epilogue above; epi == NULL is exactly
  * b200gemm_bf16_nt.  Same rules as b200gemm_bf16_nt, plus K > 0 and those in
- * the struct.  Always runs the tiled kernel (at any M); its tile width
- * accounts for the epilogue's cost (a costly epilogue favours 256-wide
- * tiles, whose epilogue overlaps the next tile's MMAs).  Every tile width
- * sums an element's K products in the same order, so the accumulator is
- * bit-identical to b200gemm_bf16_nt's whenever that call runs the tiled
- * kernel (M > 128, or the small-M kernel switched off). */
+ * the struct.  Runs the kernel b200gemm_bf16_nt would run for the shape (the
+ * small-M kernels for M <= 256, except e4m3 output with N % 16 != 0); the
+ * tiled kernel's width accounts for the epilogue's cost (a costly epilogue
+ * favours 256-wide tiles, whose epilogue overlaps the next tile's MMAs).
+ * Every tile width sums an element's K products in the same order, so the
+ * accumulator is bit-identical to b200gemm_bf16_nt's. */
 int b200gemm_bf16_nt_epilogue(b200gemm_t handle, int M, int N, int K, const void* A,
                               const void* B, void* C, int ldc, const b200gemm_epilogue* epi,
                               void* stream);
@@ -195,11 +195,13 @@ int b200gemm_plan(b200gemm_t handle, int M, int N, int K, int* plan);
  * use now; 0 for an invalid handle or shape. */
 int b200gemm_tile_width_for(b200gemm_t handle, int M, int N, int K);
 
-/* Small-M kernel (M <= 128, N % 8 == 0, K >= 128): rows of B become the MMA's
- * M side and K is split over 1, 2 or 4 CTA pairs of one cluster whose fp32
- * partial sums are reduced through distributed shared memory, so every SM
- * streams B from HBM.  mode -1 (default) or 1: use it for eligible shapes;
- * 0: always use the tiled kernel.  The reference has no small-M path. */
+/* Small-M kernels (M <= 256, N % 8 == 0, K >= 128): rows of B become the
+ * MMA's M side and K is split over 1, 2 or 4 CTA pairs of one cluster whose
+ * fp32 partial sums are reduced through distributed shared memory, so every
+ * SM streams B from HBM.  The CTA-pair form covers up to 256 rows of A, the
+ * single-CTA form up to 128.  mode -1 (default) or 1: use them for eligible
+ * shapes; 0: always use the tiled kernel.  The reference has no small-M
+ * path. */
 int b200gemm_set_small_m(b200gemm_t handle, int mode);
 
 /* Launch overlap with the previous kernel (programmatic dependent launch).

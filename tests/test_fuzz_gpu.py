@@ -62,10 +62,10 @@ def test_grid_past_16_bit_tile_coordinates_is_rejected(gpu_handle):
 
 @hyp.settings(max_examples=30, deadline=None, derandomize=True,
               suppress_health_check=list(hyp.HealthCheck))
-@hyp.given(M=st.integers(1, 128), n8=st.integers(16, 1536), k8=st.integers(16, 512),
+@hyp.given(M=st.integers(1, 256), n8=st.integers(16, 1536), k8=st.integers(16, 512),
            fused=st.booleans())
 def test_random_small_m_shapes_vs_oracle(gpu_handle, oracle_mod, M, n8, k8, fused):
-    """Decode-shaped problems (M <= 128, N a multiple of 8 up to 12288, K up
+    """Decode-shaped problems (M <= 256, N a multiple of 8 up to 12288, K up
     to 4096) through whichever small-M kernel the plan picks (pair or
     single-CTA, K split 1/2/4), plain or with a fused bias + SiLU epilogue."""
     h = gpu_handle

@@ -15,8 +15,9 @@ pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
 
 MODES = [_lib.PDL_ON, _lib.PDL_WEIGHTS_EARLY]
-# (M, K = N, plan kernel): the pair kernel, the single-CTA kernel, the tiled kernel
-CHAINS = [(128, 8192, "small_m"), (96, 4096, "small_m_1cta"), (512, 4096, "tiled")]
+# (M, K = N, plan kernel): the pair kernel, the single-CTA kernel, the tiled
+# kernel, the pair kernel covering 256 rows of A
+CHAINS = [(128, 8192, "small_m"), (96, 4096, "small_m_1cta"), (512, 4096, "tiled"), (256, 4096, "small_m")]
 STEPS = 6
 
 

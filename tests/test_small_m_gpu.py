@@ -38,6 +38,12 @@ CASES = [
     (100, 1032, 384, "small_m", 2),     # N not a multiple of 256: the last cluster is ragged
     (128, 8192, 8128, "small_m", 2),    # 127 K blocks: the last stage's second block lies past K
     (64, 16384, 320, "small_m", 1),     # 5 K blocks in stages of 2
+    # 129..256 rows of A: the pair kernel with MMA N = 256, one K block per stage
+    (256, 4096, 1024, "small_m", 2),
+    (192, 2048, 1000, "small_m", 4),    # ragged K
+    (129, 16384, 256, "small_m", 1),
+    (200, 1032, 384, "small_m", 2),     # ragged M and N
+    (256, 8192, 520, "small_m", 2),     # 9 K blocks, the last one partial
 ]
 
 
@@ -64,11 +70,12 @@ def test_small_m_parity(gpu_handle, oracle_mod, M, N, K, kernel, split):
     assert ok.all(), (np.argwhere(~ok)[:5], oracle_mod.max_scaled_error(got, ref))
 
 
-def test_small_m_unsplit_matches_tiled_bitwise(gpu_handle):
+@pytest.mark.parametrize("M", [96, 200])
+def test_small_m_unsplit_matches_tiled_bitwise(gpu_handle, M):
     """With no K split the small-M kernel sums each element in the same K
     order as the tiled kernel, so the two agree bit for bit."""
     h = gpu_handle
-    M, N, K = 96, 16384, 512
+    N, K = 16384, 512
     assert h.small_m_split(M, N, K) == 1
     A, B = data.device_operands(M, N, K, "normal", seed=5)
     C1 = h.bf16_nt(A, B)
