@@ -213,7 +213,7 @@ int b200gemm_set_small_m(b200gemm_t handle, int mode);
  * WEIGHTS_EARLY: as ON, and the first ring of B (the weights) is requested
  *   before that wait, so streaming B overlaps the previous kernel's tail.
  *   The caller guarantees that the previous kernel does not write B.
- * The tiled kernel (M > 128) takes WEIGHTS_EARLY as ON: it reads its tile
+ * The tiled kernel (M > 256) takes WEIGHTS_EARLY as ON: it reads its tile
  * table before any operand.  The multi-GPU all-gather form never overlaps.
  * Work on the stream other than these kernels (copies, events, other
  * kernels) keeps plain stream order.  The reference launches one kernel per
