@@ -421,7 +421,7 @@ struct b200gemm_handle {
   int smallm1_clusters[5] = {};       // [S]: the same for the single-CTA small-M kernel
   int tile_width = 0;         // 0 = choose per call, else one of kWidths
   int small_m = -1;           // small-M kernel: -1 or 1 = use it when eligible, 0 = never
-  int pdl = 0;                // B200GEMM_PDL_* for the small-M kernels
+  int pdl = 0;                // B200GEMM_PDL_*: launch overlap with the previous kernel
   unsigned int* status_dev = nullptr;
   unsigned long long timeout_ns = kDefaultTimeoutNs;
   int order = B200GEMM_DEFAULT_ORDER;      // tile order (schedule.cuh)
@@ -1346,42 +1346,48 @@ extern "C" int b200gemm_bf16_nt_host(b200gemm_t h, int M, int N, int K, const vo
   // never-recorded event is already complete.
   if (!ok(cudaStreamWaitEvent(st.s_h2d, buf.ev_read, 0)) || !ok(cudaStreamWaitEvent(st.s_mma, buf.ev_done, 0)))
     return B200GEMM_ERR_CUDA;
-  if (!ok(cudaEventRecord(st.ev_start, stream)) || !ok(cudaStreamWaitEvent(st.s_h2d, st.ev_start, 0)) ||
-      !ok(cudaStreamWaitEvent(st.s_mma, st.ev_start, 0)) ||
-      !ok(cudaStreamWaitEvent(st.s_d2h, st.ev_start, 0))) {
-    return B200GEMM_ERR_CUDA;
-  }
-  if (bytesB > 0 && !ok(cudaMemcpyAsync(buf.dB, hB, bytesB, cudaMemcpyHostToDevice, st.s_h2d)))
-    return B200GEMM_ERR_CUDA;
-  if (!ok(cudaEventRecord(st.ev_b, st.s_h2d)) || !ok(cudaStreamWaitEvent(st.s_mma, st.ev_b, 0)))
-    return B200GEMM_ERR_CUDA;
   auto* dA = static_cast<uint8_t*>(buf.dA);
   auto* dC = static_cast<uint8_t*>(buf.dC);
   const auto* srcA = static_cast<const uint8_t*>(hA);
   auto* dstC = static_cast<uint8_t*>(hC);
-  for (int i = 0; i < chunks; ++i) {
-    const int r0 = i * chunk_rows;
-    const int rows = (M - r0) < chunk_rows ? (M - r0) : chunk_rows;
-    const size_t a_off = static_cast<size_t>(r0) * K * 2;
-    if (K > 0 && !ok(cudaMemcpyAsync(dA + a_off, srcA + a_off, static_cast<size_t>(rows) * K * 2,
-                                     cudaMemcpyHostToDevice, st.s_h2d)))
+  auto enqueue = [&]() -> int {
+    if (!ok(cudaEventRecord(st.ev_start, stream)) || !ok(cudaStreamWaitEvent(st.s_h2d, st.ev_start, 0)) ||
+        !ok(cudaStreamWaitEvent(st.s_mma, st.ev_start, 0)) ||
+        !ok(cudaStreamWaitEvent(st.s_d2h, st.ev_start, 0))) {
       return B200GEMM_ERR_CUDA;
-    if (!ok(cudaEventRecord(st.ev_a[i], st.s_h2d)) ||
-        !ok(cudaStreamWaitEvent(st.s_mma, st.ev_a[i], 0)))
+    }
+    if (bytesB > 0 && !ok(cudaMemcpyAsync(buf.dB, hB, bytesB, cudaMemcpyHostToDevice, st.s_h2d)))
       return B200GEMM_ERR_CUDA;
-    const int rc = gemm_device(h, rows, N, K, dA + a_off, buf.dB, dC + r0 * ldc_dev * 2,
-                               static_cast<int>(ldc_dev), st.s_mma, /*allow_small_m=*/M <= 256);
-    if (rc != B200GEMM_OK) return rc;
-    if (!ok(cudaEventRecord(st.ev_c[i], st.s_mma)) ||
-        !ok(cudaStreamWaitEvent(st.s_d2h, st.ev_c[i], 0)) ||
-        !ok(cudaMemcpy2DAsync(dstC + static_cast<size_t>(r0) * ldc * 2, static_cast<size_t>(ldc) * 2,
-                              dC + r0 * ldc_dev * 2, ldc_dev * 2, static_cast<size_t>(N) * 2,
-                              static_cast<size_t>(rows), cudaMemcpyDeviceToHost, st.s_d2h)))
+    if (!ok(cudaEventRecord(st.ev_b, st.s_h2d)) || !ok(cudaStreamWaitEvent(st.s_mma, st.ev_b, 0)))
       return B200GEMM_ERR_CUDA;
-  }
-  if (!ok(cudaEventRecord(buf.ev_read, st.s_mma)) || !ok(cudaEventRecord(buf.ev_done, st.s_d2h)) ||
-      !ok(cudaStreamWaitEvent(stream, buf.ev_done, 0)))
-    return B200GEMM_ERR_CUDA;
+    for (int i = 0; i < chunks; ++i) {
+      const int r0 = i * chunk_rows;
+      const int rows = (M - r0) < chunk_rows ? (M - r0) : chunk_rows;
+      const size_t a_off = static_cast<size_t>(r0) * K * 2;
+      if (K > 0 && !ok(cudaMemcpyAsync(dA + a_off, srcA + a_off, static_cast<size_t>(rows) * K * 2,
+                                       cudaMemcpyHostToDevice, st.s_h2d)))
+        return B200GEMM_ERR_CUDA;
+      if (!ok(cudaEventRecord(st.ev_a[i], st.s_h2d)) ||
+          !ok(cudaStreamWaitEvent(st.s_mma, st.ev_a[i], 0)))
+        return B200GEMM_ERR_CUDA;
+      const int rc = gemm_device(h, rows, N, K, dA + a_off, buf.dB, dC + r0 * ldc_dev * 2,
+                                 static_cast<int>(ldc_dev), st.s_mma, /*allow_small_m=*/M <= 256);
+      if (rc != B200GEMM_OK) return rc;
+      if (!ok(cudaEventRecord(st.ev_c[i], st.s_mma)) ||
+          !ok(cudaStreamWaitEvent(st.s_d2h, st.ev_c[i], 0)) ||
+          !ok(cudaMemcpy2DAsync(dstC + static_cast<size_t>(r0) * ldc * 2, static_cast<size_t>(ldc) * 2,
+                                dC + r0 * ldc_dev * 2, ldc_dev * 2, static_cast<size_t>(N) * 2,
+                                static_cast<size_t>(rows), cudaMemcpyDeviceToHost, st.s_d2h)))
+        return B200GEMM_ERR_CUDA;
+    }
+    return B200GEMM_OK;
+  };
+  const int rc = enqueue();
+  // Whatever was enqueued, the set is reused only after it: record its
+  // events on every path (a failed call leaves the caller's stream alone).
+  const bool marked = ok(cudaEventRecord(buf.ev_read, st.s_mma)) && ok(cudaEventRecord(buf.ev_done, st.s_d2h));
+  if (rc != B200GEMM_OK) return rc;
+  if (!marked || !ok(cudaStreamWaitEvent(stream, buf.ev_done, 0))) return B200GEMM_ERR_CUDA;
   return B200GEMM_OK;
 }
 

@@ -118,9 +118,9 @@ constexpr uint32_t kEpiResidual = 2u;
 constexpr int kActNone = 0, kActRelu = 1, kActGelu = 2, kActGeluTanh = 3, kActSilu = 4;
 constexpr int kOutBf16 = 0, kOutF32 = 1, kOutE4m3 = 2;
 // Launch overlap with the previous kernel on the stream (programmatic
-// dependent launch, small-M kernels): off; on (the prologue overlaps, every
-// global access waits for the previous kernel); on with B, the weights,
-// streamed before that wait (the previous kernel must not write B).
+// dependent launch): off; on (the prologue overlaps, every global access
+// waits for the previous kernel); on with B, the weights, streamed before
+// that wait (small-M kernels only; the previous kernel must not write B).
 constexpr int kPdlOff = 0, kPdlOn = 1, kPdlWeightsEarly = 2;
 
 // One work unit of a CTA pair: a tile and a K range; slot >= 0 marks a K
