@@ -190,6 +190,10 @@ class Gemm:
         return {"kernel": kind, "tile_width": out[1], "tiles": out[2], "clusters": out[3],
                 "tail_split": out[4], "small_m_split": out[5]}
 
+    def set_tail_half(self, enable: bool) -> None:
+        """Run a short last wave of 256 x 512 tiles as 256-column halves (default on)."""
+        _lib.check(self._lib.b200gemm_set_tail_half(self._h, 1 if enable else 0), "b200gemm_set_tail_half")
+
     def set_tail_split(self, enable: bool) -> None:
         """Split the last partial wave of tiles along K (default off)."""
         _lib.check(self._lib.b200gemm_set_tail_split(self._h, 1 if enable else 0),

@@ -68,6 +68,7 @@ SIGNATURES = {
     "b200gemm_tile_width_for": (_c_int, [_vp, _c_int, _c_int, _c_int]),
     "b200gemm_set_small_m": (_c_int, [_vp, _c_int]),
     "b200gemm_set_pdl": (_c_int, [_vp, _c_int]),
+    "b200gemm_set_tail_half": (_c_int, [_vp, _c_int]),
     "b200gemm_small_m_split": (_c_int, [_vp, _c_int, _c_int, _c_int]),
     "b200gemm_set_schedule": (_c_int, [_vp, _c_int, _c_int]),
     "b200gemm_schedule_host": (_c_int, [_c_uint, _c_uint, _c_int, _c_int, ctypes.POINTER(_c_uint)]),

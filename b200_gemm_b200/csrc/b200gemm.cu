@@ -44,6 +44,8 @@ using CfgN256 = GemmCfg<B200GEMM_STAGES_N256, 1>;  // 256 x 256 tiles, overlappe
 // 256 x 512 tiles, shared A stage; 16 epilogue warps drain the single
 // 512-column accumulator (3 stages leave room for their staging buffers).
 using CfgN512 = GemmCfg<B200GEMM_STAGES_N512, 2, 256, false, B200GEMM_EPIWARPS_N512>;
+// The same tiles, launched only when a short last wave runs as 256-column halves.
+using CfgN512H = GemmCfg<B200GEMM_STAGES_N512, 2, 256, false, B200GEMM_EPIWARPS_N512, true>;
 // Narrower tiles for N that 256 does not divide into full waves (e.g. an
 // N-sharded projection with N = 1792 = 8 x 224); more stages fit because each
 // stage holds fewer B rows.
@@ -334,19 +336,26 @@ cudaError_t launch_gemm(int clusters, cudaStream_t stream, const CUtensorMap& ma
 // per flop as the 256-wide tile's and the epilogue costs 17 K blocks.
 // `epi` adds the fused epilogue's measured per-tile cost (epilogue_cost).
 double tile_plan_cost(int width, uint32_t tiles_m, int N, int num_kb, int clusters,
-                      double epi = 0.0) {
+                      double epi = 0.0, bool half_tail = false) {
   if (clusters <= 0) return 1e300;
   const uint64_t tiles_n = (static_cast<uint64_t>(N) + width - 1) / width;
   const uint64_t tiles = tiles_m * tiles_n;
   const uint64_t waves = (tiles + clusters - 1) / clusters;
-  double tile_time;
+  auto narrow_time = [&](int w) {
+    const double feed = (16384.0 + 64.0 * w) / 32768.0;
+    return num_kb * (0.08 + 0.92 * feed) / 0.85;
+  };
   if (width == 512) {
-    tile_time = (2.0 * num_kb + 17.0) * 0.8545 / 0.85;
-  } else {
-    const double feed = (16384.0 + 64.0 * width) / 32768.0;
-    tile_time = num_kb * (0.08 + 0.92 * feed) / 0.85;
+    const double tile_time = (2.0 * num_kb + 17.0) * 0.8545 / 0.85;
+    const uint64_t rem = tiles % static_cast<uint64_t>(clusters);
+    if (half_tail && epi == 0.0 && rem > 0 && 2 * rem <= static_cast<uint64_t>(clusters)) {
+      // The last wave runs as 256-column halves, measured at 0.84 of a whole
+      // tile's time (the 3-stage ring holds fewer bytes in flight for them).
+      return (static_cast<double>(waves - 1) + 0.84) * tile_time;
+    }
+    return static_cast<double>(waves) * (tile_time + epi);
   }
-  return static_cast<double>(waves) * (tile_time + epi);
+  return static_cast<double>(waves) * (narrow_time(width) + epi);
 }
 
 // Per-tile cost of a fused epilogue, in tile_plan_cost's units, measured on
@@ -439,6 +448,7 @@ struct b200gemm_handle {
   cudaEvent_t tail_event = nullptr;
   bool tail_event_recorded = false;
   bool tail_split_enabled = false;  // off by default until its reduction beats the idle wave
+  bool tail_half_enabled = true;    // 256 x 512 tiles: a short last wave as half-width tiles
   std::mutex staging_mu;   // serialises b200gemm_bf16_nt_host calls on one handle
   std::vector<ScheduleEntry> schedules;
 };
@@ -482,6 +492,7 @@ extern "C" int b200gemm_create(b200gemm_t* out, int device) {
                               prepare_kernel<CfgE128>(sms)};
   for (int i = 0; i < kNumWidths; ++i)
     if (cw[i] <= 0 || ce[i] <= 0) return B200GEMM_ERR_CUDA;
+  if (prepare_kernel<CfgN512H>(sms) <= 0) return B200GEMM_ERR_CUDA;
   const int dc1 = prepare_decode_kernel<DecodeCfg<1>>(sms), dc2 = prepare_decode_kernel<DecodeCfg<2>>(sms),
             dc4 = prepare_decode_kernel<DecodeCfg<4>>(sms);
   if (dc1 <= 0 || dc2 <= 0 || dc4 <= 0) return B200GEMM_ERR_CUDA;
@@ -666,6 +677,15 @@ namespace {
 
 bool tail_split_enabled_for(const b200gemm_handle* h) { return h->tail_split_enabled; }
 
+// Tiles of the last wave that run as 256-column halves (0 = none): with T
+// 256 x 512 tiles on G clusters, the R = T mod G tiles of the last wave when
+// 2R <= G (a single partial wave counts: R = T < G).
+int tail_half_for(const b200gemm_handle* h, int tiles, int clusters) {
+  if (!h->tail_half_enabled || clusters <= 0) return 0;
+  const int rem = tiles % clusters;
+  return (rem > 0 && 2 * rem <= clusters) ? rem : 0;
+}
+
 // Instances that carry the K-split tail (GemmCfg::kTailSplit): the plain
 // ones except the 512-wide, whose 16 epilogue warps leave it no registers.
 bool tail_split_width(int width, bool fused) {
@@ -691,6 +711,12 @@ int choose_tile_width(const b200gemm_handle* h, int M, int N, int K,
       best = kWidths[i];
     }
   }
+  // 256 x 512 tiles with a half-width last wave replace the choice only when
+  // clearly cheaper (3%): the model's margin of error is about that.
+  if (best != 512 && h->tail_half_enabled && epi == nullptr) {
+    const double c = tile_plan_cost(512, tiles_m, N, num_kb, clusters[width_index(512)], 0.0, true);
+    if (c < 0.97 * best_cost) best = 512;
+  }
   return best;
 }
 
@@ -710,7 +736,9 @@ cudaError_t launch_width(int width, bool fused, int clusters, cudaStream_t strea
     }
   }
   switch (width) {
-    case 512: return launch_gemm<CfgN512>(clusters, stream, ma, mb, mc, p);
+    case 512:
+      return p.tail_half ? launch_gemm<CfgN512H>(clusters, stream, ma, mb, mc, p)
+                         : launch_gemm<CfgN512>(clusters, stream, ma, mb, mc, p);
     case 224: return launch_gemm<CfgN224>(clusters, stream, ma, mb, mc, p);
     case 192: return launch_gemm<CfgN192>(clusters, stream, ma, mb, mc, p);
     case 128: return launch_gemm<CfgN128>(clusters, stream, ma, mb, mc, p);
@@ -1139,6 +1167,16 @@ int gemm_device(b200gemm_t h, int M, int N, int K, const void* A, const void* B,
     }
   }
 
+  // 256 x 512 tiles: a last wave of at most half as many tiles as clusters
+  // runs as 256-column halves on twice the clusters (plain epilogue only).
+  if (!tail_on && width == 512 && !fused && tail_half_for(h, p.num_tiles, max_clusters) > 0) {
+    const int rem = tail_half_for(h, p.num_tiles, max_clusters);
+    p.tail_start = p.num_tiles - rem;
+    p.tail_half = 1;
+    p.num_units = p.tail_start + 2 * rem;
+    clusters = p.num_units < max_clusters ? p.num_units : max_clusters;
+  }
+
   const cudaError_t e = launch_width(width, fused, clusters, stream, ma, mb, mc, p);
   if (e == cudaSuccess && tail_on) {
     std::lock_guard<std::mutex> lock(h->mu);
@@ -1168,13 +1206,21 @@ extern "C" int b200gemm_plan(b200gemm_t h, int M, int N, int K, int* plan) {
   const int maxc = h->clusters_w[width_index(width)];
   const int num_kb = (K + kBlockK - 1) / kBlockK;
   const int sk = (h->tail_split_enabled && tail_split_width(width, false)) ? tail_split_for(tiles, maxc, num_kb) : 1;
-  const int units = tiles + (sk >= 2 ? (tiles % maxc) * (sk - 1) : 0);
+  const int halves = (sk < 2 && width == 512) ? tail_half_for(h, tiles, maxc) : 0;
+  const int units = tiles + (sk >= 2 ? (tiles % maxc) * (sk - 1) : 0) + halves;
   const int clusters = units < maxc ? units : maxc;
   plan[0] = 1;  // tiled kernel
   plan[1] = width;
   plan[2] = tiles;
   plan[3] = clusters;
-  plan[4] = sk;
+  plan[4] = sk >= 2 ? sk : (halves > 0 ? -2 : 1);
+  return B200GEMM_OK;
+}
+
+extern "C" int b200gemm_set_tail_half(b200gemm_t h, int enable) {
+  if (h == nullptr) return B200GEMM_ERR_INVALID_ARG;
+  std::lock_guard<std::mutex> lock(h->mu);
+  h->tail_half_enabled = enable != 0;
   return B200GEMM_OK;
 }
 

@@ -93,10 +93,15 @@ struct GemmParams {
   // tail_kb K blocks) of tile tiles[tail_start + r].  A K slice writes its
   // fp32 partial to workspace and takes a ticket from tail_counters; the last
   // of a tile's slices adds the others to its own accumulator and stores C.
-  int num_units;        // tail_start + tail_tiles * tail_split
+  int num_units;        // tail_start + tail_tiles * tail_split (or * 2 with tail_half)
   int tail_start;
   int tail_split;       // 1 = no split
   int tail_kb;
+  // 256 x 512 tiles only: with tail_half, unit tail_start + 2 r + h is the
+  // h-th 256-column half of tile tiles[tail_start + r] over the whole of K,
+  // so a last wave of up to half the clusters' tiles runs in about half a
+  // tile's time on twice the clusters.
+  int tail_half;
   float* workspace;     // [tail unit][CTA of the pair][128 rows x tile width] fp32
   unsigned int* tail_counters;  // [tail tile][CTA of the pair], zero between launches
   // Fused epilogue (instances with Cfg::kEpi only), per element in fp32:
@@ -124,13 +129,18 @@ constexpr int kOutBf16 = 0, kOutF32 = 1, kOutE4m3 = 2;
 constexpr int kPdlOff = 0, kPdlOn = 1, kPdlWeightsEarly = 2;
 
 // One work unit of a CTA pair: a tile and a K range; slot >= 0 marks a K
-// slice of a split tile (its index among the tail units).
+// slice of a split tile (its index among the tail units), slot -2 - h the
+// h-th 256-column half of a 256 x 512 tile, slot -1 a whole tile.
 struct WorkUnit {
   uint32_t tile;
   int kb_begin, kb_end;
   int slot;
 };
 
+// Which 256-column half of a 256 x 512 tile a unit covers (-1: all of it).
+__device__ __forceinline__ int unit_half(const WorkUnit& w) { return w.slot <= -2 ? -2 - w.slot : -1; }
+
+template <bool HALF>
 __device__ __forceinline__ WorkUnit unit_at(const GemmParams& p, uint32_t u) {
   WorkUnit w;
   if (u < static_cast<uint32_t>(p.tail_start)) {
@@ -138,6 +148,12 @@ __device__ __forceinline__ WorkUnit unit_at(const GemmParams& p, uint32_t u) {
     w.kb_begin = 0;
     w.kb_end = p.num_kb;
     w.slot = -1;
+  } else if (HALF) {
+    const int v = static_cast<int>(u) - p.tail_start;
+    w.tile = __ldg(p.tiles + p.tail_start + (v >> 1));
+    w.kb_begin = 0;
+    w.kb_end = p.num_kb;
+    w.slot = -2 - (v & 1);
   } else {
     const int v = static_cast<int>(u) - p.tail_start;
     const int r = v / p.tail_split, sl = v - r * p.tail_split;
@@ -165,13 +181,17 @@ __device__ __forceinline__ WorkUnit unit_at(const GemmParams& p, uint32_t u) {
 //           More warps drain a single (non double-buffered) accumulator
 //           sooner: every warp's chunks run as one serial chain of TMEM load,
 //           staging and TMA store.
-template <int STAGES, int NB, int MN = 256, bool EPI = false, int EW = 4 * NB>
+template <int STAGES, int NB, int MN = 256, bool EPI = false, int EW = 4 * NB, bool HALF = false>
 struct GemmCfg {
   static_assert(NB == 1 || NB == 2, "one or two MMA column blocks per tile");
   static_assert(MN % 32 == 0 && MN >= 64 && MN <= 256 && (NB == 1 || MN == 256), "MMA width");
   static constexpr int kStages = STAGES;
   static constexpr int kNB = NB;
   static constexpr bool kEpi = EPI;
+  // Instances that run a short last wave as 256-column halves (tail_half);
+  // a separate instance, so the others carry none of its code.
+  static constexpr bool kHalfTail = HALF;
+  static_assert(!HALF || (NB == 2 && !EPI), "half-width units are 256 x 512 plain tiles");
   static constexpr int kMmaN = MN;                       // columns per tcgen05.mma
   static constexpr int kBRows = MN / 2;                  // B rows per CTA per column block
   static constexpr int kBlockBytesB = kBRows * kBlockK * 2;
@@ -623,10 +643,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
       const uint32_t full_leader0 = ptx::mapa(full0, 0);
       uint32_t stage = 0, phase = 0;
       bool ok = true;
-      WorkUnit nxt = (cluster < num_units) ? unit_at(p, cluster) : WorkUnit{0, 0, 0, -1};
+      WorkUnit nxt = (cluster < num_units) ? unit_at<Cfg::kHalfTail>(p, cluster) : WorkUnit{0, 0, 0, -1};
       for (uint32_t t = cluster; t < num_units && ok; t += nclusters) {
         const WorkUnit cur = nxt;
-        if (t + nclusters < num_units) nxt = unit_at(p, t + nclusters);
+        if (t + nclusters < num_units) nxt = unit_at<Cfg::kHalfTail>(p, t + nclusters);
         const uint32_t tile = cur.tile;
         const int row_a = static_cast<int>(tile >> 16) * kTileM + static_cast<int>(rank) * 128;
         const int row_b =
@@ -636,13 +656,19 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
             ok = false;
             break;
           }
-          if (leader) ptx::mbar_arrive_expect_tx(full0 + 8 * stage, Cfg::kTxBytes);
+          // A half unit loads its one 256-column block of B into slot 0.
+          const int half = Cfg::kHalfTail ? unit_half(cur) : -1;
+          const bool half_unit = Cfg::kHalfTail && half >= 0;
+          if (leader)
+            ptx::mbar_arrive_expect_tx(full0 + 8 * stage,
+                                       half_unit ? 2u * (kStageBytesA + Cfg::kBlockBytesB) : Cfg::kTxBytes);
           const uint32_t fb = full_leader0 + 8 * stage;
           ptx::tma_load_2d_cg2(sA + stage * kStageBytesA, &map_a, fb, kb * kBlockK, row_a, policy_a);
 #pragma unroll
           for (int h = 0; h < NB; ++h) {
+            if (half_unit && h > 0) break;
             ptx::tma_load_2d_cg2(sB + stage * Cfg::kStageBytesB + h * Cfg::kBlockBytesB, &map_b, fb,
-                                 kb * kBlockK, row_b + h * Cfg::kMmaN, policy_b);
+                                 kb * kBlockK, row_b + (half_unit ? half : h) * Cfg::kMmaN, policy_b);
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -661,7 +687,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
       uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
       bool ok = true;
       for (uint32_t t = cluster; t < num_units && ok; t += nclusters) {
-        const WorkUnit cur = unit_at(p, t);
+        const WorkUnit cur = unit_at<Cfg::kHalfTail>(p, t);
         if (!ptx::mbar_wait(tempty0 + 8 * acc, acc_phase ^ 1u, wd, kSiteMmaTmemEmpty, t)) break;
         ptx::tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * Cfg::kAccStride;
@@ -673,10 +699,12 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
           ptx::tc_fence_after();
           const uint64_t a_desc = smem_desc(sA + stage * kStageBytesA);
           const uint64_t b_desc = smem_desc(sB + stage * Cfg::kStageBytesB);
+          const int nb_now = (Cfg::kHalfTail && cur.slot <= -2) ? 1 : NB;  // a half unit: columns 0..255
 #pragma unroll
           for (int k = 0; k < kBlockK / kMmaK; ++k) {
 #pragma unroll
             for (int h = 0; h < NB; ++h) {
+              if (h >= nb_now) break;
               // +32 bytes per K step inside the 128-byte swizzle row; the
               // second N block of B sits kBlockBytesB further on.
               ptx::mma_bf16_cg2(d_tmem + h * Cfg::kMmaN, a_desc + 2 * k,
@@ -717,14 +745,20 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
     const uint32_t tempty_leader0 = ptx::mapa(tempty0, 0);
     uint32_t acc = 0, acc_phase = 0, cbuf = 0;
     const uint32_t ticket = base + Cfg::kTicket;
-    WorkUnit nxt = (cluster < num_units) ? unit_at(p, cluster) : WorkUnit{0, 0, 0, -1};
+    WorkUnit nxt = (cluster < num_units) ? unit_at<Cfg::kHalfTail>(p, cluster) : WorkUnit{0, 0, 0, -1};
     for (uint32_t t = cluster; t < num_units; t += nclusters) {
       const WorkUnit cur = nxt;
-      if (t + nclusters < num_units) nxt = unit_at(p, t + nclusters);
+      if (t + nclusters < num_units) nxt = unit_at<Cfg::kHalfTail>(p, t + nclusters);
       const uint32_t tile = cur.tile;
       const int row = static_cast<int>(tile >> 16) * kTileM + static_cast<int>(rank) * 128 +
                       static_cast<int>(quarter) * 32;
-      const int col0 = static_cast<int>(tile & 0xFFFFu) * Cfg::kTileN + static_cast<int>(nblk) * Cfg::kColsPerWarp;
+      // A half unit's accumulator is TMEM columns 0..255 for global columns
+      // half * 256 ..; the warps holding columns 256..511 have nothing.
+      const int half = Cfg::kHalfTail ? unit_half(cur) : -1;
+      const int half_off = half >= 0 ? half * Cfg::kMmaN : 0;
+      const bool idle_half = half >= 0 && static_cast<int>(nblk) * Cfg::kColsPerWarp >= Cfg::kMmaN;
+      const int col0 = static_cast<int>(tile & 0xFFFFu) * Cfg::kTileN + half_off +
+                       static_cast<int>(nblk) * Cfg::kColsPerWarp;
       [[maybe_unused]] uint32_t bias_w[4];
       [[maybe_unused]] uint32_t res_w[16];
       if constexpr (Cfg::kEpi) {
@@ -752,6 +786,11 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
           tmem_base + ((quarter * 32u) << 16) + acc * Cfg::kAccStride + nblk * Cfg::kColsPerWarp;
       if (cur.slot < 0 && !live) {
         // nothing to do for this tile
+      } else if (idle_half) {
+        // Columns this warp would drain belong to no tile in a half unit.
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive_cluster(tempty_leader0 + 8 * acc);
       } else if (cur.slot < 0) {
         // Whole tile: chunks of 32 columns: TMEM -> registers -> bf16 ->
         // swizzled staging buffer -> TMA store, two buffers in flight per warp.

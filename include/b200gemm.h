@@ -184,11 +184,19 @@ int b200gemm_set_tile_width(b200gemm_t handle, int width);
  * an event (they share the workspace).  No reference counterpart. */
 int b200gemm_set_tail_split(b200gemm_t handle, int enable);
 
+/* Run a short last wave of 256 x 512 tiles as 256-column halves (default
+ * on): when T tiles leave R = T mod G of G clusters busy in the last wave and
+ * 2R <= G, each of those R tiles runs as two half tiles over the whole of K on
+ * 2R clusters, so that wave takes about half a tile's time.  Plain epilogue
+ * only.  No reference counterpart (its tiles are always 256 x 256). */
+int b200gemm_set_tail_half(b200gemm_t handle, int enable);
+
 /* Launch plan a call with this shape would use now, in plan[0..5]: kernel
  * (1 tiled, 2 small-M with 256 rows of B per CTA pair, 3 small-M with 128
  * rows of B per CTA), tile width (tiled) or rows of B per cluster (small-M),
- * tiles, clusters launched, K split of the last partial wave (1 = none;
- * tiled kernel), K split of the small-M kernel. */
+ * tiles, clusters launched, how the tiles of the last partial wave are cut
+ * (tiled kernel: 1 = not at all, S >= 2 = into S K slices, -2 = into two
+ * 256-column halves), K split of the small-M kernel. */
 int b200gemm_plan(b200gemm_t handle, int M, int N, int K, int* plan);
 
 /* The tile width (512, 256, 224, 192 or 128) a call with this shape would

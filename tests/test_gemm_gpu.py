@@ -137,6 +137,11 @@ def test_tile_width_selection(gpu_handle):
     assert h.tile_width_for(256, 256, 64) in WIDTHS
     # N-sharded MLP projection: 1792 = 8 x 224 columns fill the last wave
     assert h.tile_width_for(16384, 1792, 4096) == 224
+    # 16384^3 sharded over 8 GPUs: 256 x 512 tiles with their 34-tile last
+    # wave cut into 256-column halves; short K keeps 256-wide tiles
+    assert h.tile_width_for(16384, 2048, 16384) == 512
+    assert h.plan(16384, 2048, 16384)["tail_split"] == -2
+    assert h.tile_width_for(16384, 2048, 4096) == 256
     for w in WIDTHS:
         h.set_tile_width(w)
         assert h.tile_width_for(256, 256, 64) == w

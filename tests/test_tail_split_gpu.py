@@ -64,12 +64,18 @@ def test_tail_split_parity(gpu_handle, oracle_mod, M, N, K, width):
 
 
 def test_no_tail_split_at_width_512(gpu_handle):
+    """The 256 x 512 instance carries no K-split tail: its short last wave is
+    cut into 256-column halves instead (b200gemm_set_tail_half), or not at all."""
     h = gpu_handle
     h.set_tile_width(512)
     h.set_tail_split(True)
     try:
-        plan = h.plan(16384, 2048, 2048)
+        plan_halves = h.plan(16384, 2048, 2048)
+        h.set_tail_half(False)
+        plan_none = h.plan(16384, 2048, 2048)
     finally:
         h.set_tile_width(0)
         h.set_tail_split(False)
-    assert plan["tile_width"] == 512 and plan["tail_split"] == 1
+        h.set_tail_half(True)
+    assert plan_halves["tile_width"] == 512 and plan_halves["tail_split"] == -2
+    assert plan_none["tile_width"] == 512 and plan_none["tail_split"] == 1
