@@ -183,7 +183,9 @@ class Gemm:
         return out
 
     def plan(self, M: int, N: int, K: int) -> dict:
-        """How a call with this shape would run on this handle now."""
+        """How a call with this shape would run on this handle now.  For the
+        tiled kernel, tail_split tells how the tiles of a partial last wave are
+        cut: 1 not at all, S >= 2 into S K slices, -2 into two 256-column halves."""
         out = (ctypes.c_int * 6)()
         _lib.check(self._lib.b200gemm_plan(self._h, M, N, K, out), "b200gemm_plan")
         kind = {1: "tiled", 2: "small_m", 3: "small_m_1cta"}.get(out[0], "?")
