@@ -19,7 +19,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, M, N, K, q):
+def _worker(rank, world, port, M, N, K, width, q):
     import datetime
 
     import torch.distributed as dist
@@ -33,6 +33,8 @@ def _worker(rank, world, port, M, N, K, q):
                             timeout=datetime.timedelta(seconds=60))
     try:
         gemm = Gemm(rank)
+        if width:
+            gemm.set_tile_width(width)
         A, B = data.device_operands(M, N, K, "normal", seed=11, device=f"cuda:{rank}")
         fused = shard.FusedAllGather(gemm, M, N)
         n0, n1 = fused.n0, fused.n1
@@ -57,8 +59,10 @@ def _worker(rank, world, port, M, N, K, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("M,N,K", [(1024, 2048, 512), (600, 1536, 264)])
-def test_fused_allgather_matches_single_gpu(M, N, K):
+# width 512 on these shapes puts every rank's few 256 x 512 tiles in one short
+# wave, which runs as 256-column halves whose epilogue also writes the peers.
+@pytest.mark.parametrize("M,N,K,width", [(1024, 2048, 512, 0), (600, 1536, 264, 0), (1024, 2048, 512, 512)])
+def test_fused_allgather_matches_single_gpu(M, N, K, width):
     n = torch.cuda.device_count()
     if n < 2:
         pytest.skip("needs at least two GPUs")
@@ -66,7 +70,7 @@ def test_fused_allgather_matches_single_gpu(M, N, K):
     ctx = torch.multiprocessing.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, M, N, K, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, M, N, K, width, q)) for r in range(world)]
     for p in procs:
         p.start()
     results = {}
