@@ -40,6 +40,8 @@ WORKLOADS = {
     # name: global shape, operand distribution, how N>1 shards it
     "square8192": dict(M=8192, N=8192, K=8192, dist="uniform", scaling="weak"),
     "square16384": dict(M=16384, N=16384, K=16384, dist="normal", scaling="strong"),
+    # one GPU's part of square16384 on 8 GPUs (N = 16384 / 8 columns)
+    "shard16384x8": dict(M=16384, N=2048, K=16384, dist="normal", scaling="weak"),
     "mlp": dict(M=16384, N=14336, K=4096, dist="mlp", scaling="strong"),
     # Decode shapes run as a decoder runs them: back to back, each step on the
     # next of `weights` weight matrices (B), whose total exceeds twice L2, with
