@@ -228,7 +228,15 @@ struct GemmCfg {
   static constexpr int kC = kB + STAGES * kStageBytesB;
   static constexpr int kFull = kC + kEpiWarps * kCBufs * kCStageBytes;
   static constexpr int kEmpty = kFull + 8 * STAGES;
-  static constexpr int kTFull = kEmpty + 8 * STAGES;
+  // Half units (kHalfTail) move one B block per K block, so once a CTA's
+  // whole tiles are done its ring is re-cut into kHalfStages stages of
+  // kHalfStageBytes (A, then the B block) over the same bytes, with their own
+  // barriers: more bytes in flight than the whole-tile stages would carry.
+  static constexpr int kHalfStageBytes = kStageBytesA + kBlockBytesB;
+  static constexpr int kHalfStages = HALF ? STAGES * (kStageBytesA + kStageBytesB) / kHalfStageBytes : 0;
+  static constexpr int kFull2 = kEmpty + 8 * STAGES;
+  static constexpr int kEmpty2 = kFull2 + 8 * kHalfStages;
+  static constexpr int kTFull = kEmpty2 + 8 * kHalfStages;
   static constexpr int kTEmpty = kTFull + 8 * kAccBufs;
   static constexpr int kDrain = kTEmpty + 8 * kAccBufs;
   static constexpr int kTmemSlot = kDrain + 8;
@@ -609,6 +617,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
       ptx::mbar_init(full0 + 8 * s, 1);   // leader's expect_tx arrival (+ bytes of both CTAs)
       ptx::mbar_init(empty0 + 8 * s, 1);  // one MMA commit
     }
+    for (int s = 0; s < Cfg::kHalfStages; ++s) {
+      ptx::mbar_init(base + Cfg::kFull2 + 8 * s, 1);
+      ptx::mbar_init(base + Cfg::kEmpty2 + 8 * s, 1);
+    }
     for (int a = 0; a < Cfg::kAccBufs; ++a) {
       ptx::mbar_init(tfull0 + 8 * a, 1);                     // one MMA commit
       ptx::mbar_init(tempty0 + 8 * a, 2 * Cfg::kEpiWarps);   // every epilogue warp of the pair
@@ -642,6 +654,8 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
       const uint64_t policy_b = ptx::l2_policy(B200GEMM_L2_POLICY_B);
       const uint32_t full_leader0 = ptx::mapa(full0, 0);
       uint32_t stage = 0, phase = 0;
+      [[maybe_unused]] uint32_t hstage = 0, hphase = 0;
+      [[maybe_unused]] bool half_ring = false;
       bool ok = true;
       WorkUnit nxt = (cluster < num_units) ? unit_at<Cfg::kHalfTail>(p, cluster) : WorkUnit{0, 0, 0, -1};
       for (uint32_t t = cluster; t < num_units && ok; t += nclusters) {
@@ -651,24 +665,54 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
         const int row_a = static_cast<int>(tile >> 16) * kTileM + static_cast<int>(rank) * 128;
         const int row_b =
             static_cast<int>(tile & 0xFFFFu) * Cfg::kTileN + static_cast<int>(rank) * Cfg::kBRows;
+        if constexpr (Cfg::kHalfTail) {
+          if (cur.slot <= -2) {
+            // Half units come after this CTA's whole tiles.  Before the ring
+            // is re-cut, every whole-tile stage must have been consumed.
+            if (!half_ring) {
+              for (int s = 0; s < STAGES && ok; ++s) {
+                if (!ptx::mbar_wait(empty0 + 8 * stage, phase ^ 1u, wd, kSiteProducer, t)) ok = false;
+                if (++stage == STAGES) {
+                  stage = 0;
+                  phase ^= 1u;
+                }
+              }
+              half_ring = true;
+              if (!ok) break;
+            }
+            const uint32_t full2 = base + Cfg::kFull2, empty2 = base + Cfg::kEmpty2;
+            const uint32_t full2_leader = ptx::mapa(full2, 0);
+            const int rb = row_b + unit_half(cur) * Cfg::kMmaN;  // the 256-column block of B
+            for (int kb = cur.kb_begin; kb < cur.kb_end; ++kb) {
+              if (!ptx::mbar_wait(empty2 + 8 * hstage, hphase ^ 1u, wd, kSiteProducer, t)) {
+                ok = false;
+                break;
+              }
+              if (leader) ptx::mbar_arrive_expect_tx(full2 + 8 * hstage, 2u * Cfg::kHalfStageBytes);
+              const uint32_t fb = full2_leader + 8 * hstage;
+              const uint32_t dst = sA + hstage * Cfg::kHalfStageBytes;
+              ptx::tma_load_2d_cg2(dst, &map_a, fb, kb * kBlockK, row_a, policy_a);
+              ptx::tma_load_2d_cg2(dst + kStageBytesA, &map_b, fb, kb * kBlockK, rb, policy_b);
+              if (++hstage == static_cast<uint32_t>(Cfg::kHalfStages)) {
+                hstage = 0;
+                hphase ^= 1u;
+              }
+            }
+            continue;
+          }
+        }
         for (int kb = cur.kb_begin; kb < cur.kb_end; ++kb) {
           if (!ptx::mbar_wait(empty0 + 8 * stage, phase ^ 1u, wd, kSiteProducer, t)) {
             ok = false;
             break;
           }
-          // A half unit loads its one 256-column block of B into slot 0.
-          const int half = Cfg::kHalfTail ? unit_half(cur) : -1;
-          const bool half_unit = Cfg::kHalfTail && half >= 0;
-          if (leader)
-            ptx::mbar_arrive_expect_tx(full0 + 8 * stage,
-                                       half_unit ? 2u * (kStageBytesA + Cfg::kBlockBytesB) : Cfg::kTxBytes);
+          if (leader) ptx::mbar_arrive_expect_tx(full0 + 8 * stage, Cfg::kTxBytes);
           const uint32_t fb = full_leader0 + 8 * stage;
           ptx::tma_load_2d_cg2(sA + stage * kStageBytesA, &map_a, fb, kb * kBlockK, row_a, policy_a);
 #pragma unroll
           for (int h = 0; h < NB; ++h) {
-            if (half_unit && h > 0) break;
             ptx::tma_load_2d_cg2(sB + stage * Cfg::kStageBytesB + h * Cfg::kBlockBytesB, &map_b, fb,
-                                 kb * kBlockK, row_b + (half_unit ? half : h) * Cfg::kMmaN, policy_b);
+                                 kb * kBlockK, row_b + h * Cfg::kMmaN, policy_b);
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -685,12 +729,50 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
       const uint32_t own_empty0 = ptx::mapa(empty0, 0), peer_empty0 = ptx::mapa(empty0, 1);
       const uint32_t own_tfull0 = ptx::mapa(tfull0, 0), peer_tfull0 = ptx::mapa(tfull0, 1);
       uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+      [[maybe_unused]] uint32_t hstage = 0, hphase = 0;
       bool ok = true;
       for (uint32_t t = cluster; t < num_units && ok; t += nclusters) {
         const WorkUnit cur = unit_at<Cfg::kHalfTail>(p, t);
         if (!ptx::mbar_wait(tempty0 + 8 * acc, acc_phase ^ 1u, wd, kSiteMmaTmemEmpty, t)) break;
         ptx::tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * Cfg::kAccStride;
+        if constexpr (Cfg::kHalfTail) {
+          if (cur.slot <= -2) {
+            // Half unit: the re-cut ring, one N = 256 MMA per K step into
+            // TMEM columns 0..255.
+            const uint32_t full2 = base + Cfg::kFull2, empty2 = base + Cfg::kEmpty2;
+            const uint32_t own_empty2 = ptx::mapa(empty2, 0), peer_empty2 = ptx::mapa(empty2, 1);
+            for (int kb = cur.kb_begin; kb < cur.kb_end; ++kb) {
+              if (!ptx::mbar_wait(full2 + 8 * hstage, hphase, wd, kSiteMmaFull, t)) {
+                ok = false;
+                break;
+              }
+              ptx::tc_fence_after();
+              const uint32_t src = sA + hstage * Cfg::kHalfStageBytes;
+              const uint64_t a_desc = smem_desc(src);
+              const uint64_t b_desc = smem_desc(src + kStageBytesA);
+#pragma unroll
+              for (int k = 0; k < kBlockK / kMmaK; ++k) {
+                ptx::mma_bf16_cg2(d_tmem, a_desc + 2 * k, b_desc + 2 * k, Cfg::kIdesc,
+                                  (kb > cur.kb_begin || k > 0) ? 1u : 0u);
+              }
+              ptx::mma_commit_cg2(own_empty2 + 8 * hstage);
+              ptx::mma_commit_cg2(peer_empty2 + 8 * hstage);
+              if (++hstage == static_cast<uint32_t>(Cfg::kHalfStages)) {
+                hstage = 0;
+                hphase ^= 1u;
+              }
+            }
+            if (!ok) break;
+            ptx::mma_commit_cg2(own_tfull0 + 8 * acc);
+            ptx::mma_commit_cg2(peer_tfull0 + 8 * acc);
+            if (++acc == Cfg::kAccBufs) {
+              acc = 0;
+              acc_phase ^= 1u;
+            }
+            continue;
+          }
+        }
         for (int kb = cur.kb_begin; kb < cur.kb_end; ++kb) {
           if (!ptx::mbar_wait(full0 + 8 * stage, phase, wd, kSiteMmaFull, t)) {
             ok = false;
@@ -699,12 +781,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
           ptx::tc_fence_after();
           const uint64_t a_desc = smem_desc(sA + stage * kStageBytesA);
           const uint64_t b_desc = smem_desc(sB + stage * Cfg::kStageBytesB);
-          const int nb_now = (Cfg::kHalfTail && cur.slot <= -2) ? 1 : NB;  // a half unit: columns 0..255
 #pragma unroll
           for (int k = 0; k < kBlockK / kMmaK; ++k) {
 #pragma unroll
             for (int h = 0; h < NB; ++h) {
-              if (h >= nb_now) break;
               // +32 bytes per K step inside the 128-byte swizzle row; the
               // second N block of B sits kBlockBytesB further on.
               ptx::mma_bf16_cg2(d_tmem + h * Cfg::kMmaN, a_desc + 2 * k,
