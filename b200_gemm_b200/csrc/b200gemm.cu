@@ -349,9 +349,9 @@ double tile_plan_cost(int width, uint32_t tiles_m, int N, int num_kb, int cluste
     const double tile_time = (2.0 * num_kb + 17.0) * 0.8545 / 0.85;
     const uint64_t rem = tiles % static_cast<uint64_t>(clusters);
     if (half_tail && epi == 0.0 && rem > 0 && 2 * rem <= static_cast<uint64_t>(clusters)) {
-      // The last wave runs as 256-column halves, measured at 0.84 of a whole
-      // tile's time (the 3-stage ring holds fewer bytes in flight for them).
-      return (static_cast<double>(waves - 1) + 0.84) * tile_time;
+      // The last wave runs as 256-column halves on their own 4-stage ring:
+      // about 0.45-0.65 of a whole tile's cycles in ncu captures; 0.6 here.
+      return (static_cast<double>(waves - 1) + 0.6) * tile_time;
     }
     return static_cast<double>(waves) * (tile_time + epi);
   }

@@ -142,6 +142,7 @@ def test_tile_width_selection(gpu_handle):
     assert h.tile_width_for(16384, 2048, 16384) == 512
     assert h.plan(16384, 2048, 16384)["tail_split"] == -2
     assert h.tile_width_for(16384, 2048, 4096) == 256
+    assert h.tile_width_for(4096, 8192, 8192) == 512  # 256 tiles, a 34-tile last wave in halves
     for w in WIDTHS:
         h.set_tile_width(w)
         assert h.tile_width_for(256, 256, 64) == w
