@@ -1509,6 +1509,14 @@ extern "C" int b200gemm_bf16_nt_noalloc(int M, int N, int K, const void* A, cons
       const int c256 = prepare_kernel<CfgN256>(sms);
       const int c512 = prepare_kernel<CfgN512>(sms);
       if (c256 <= 0 || c512 <= 0) return B200GEMM_ERR_CUDA;
+      // Load the schedule kernel's module now as well: with lazy module
+      // loading its first launch would otherwise load it, which can allocate
+      // device memory, on whichever later call first reaches that launch.
+      cudaFuncAttributes fa;
+      if (cudaFuncGetAttributes(&fa, build_schedule_kernel) != cudaSuccess) {
+        cudaGetLastError();
+        return B200GEMM_ERR_CUDA;
+      }
       d.scratch = static_cast<uint32_t*>(ptr);
       d.clusters_n256 = c256;
       d.clusters_n512 = c512;

@@ -12,6 +12,9 @@ MLP shape over 8 GPUs).
 """
 from __future__ import annotations
 
+import contextlib
+import os
+
 TILE_N = 256  # shard boundaries fall on kernel tile boundaries
 
 
@@ -53,6 +56,132 @@ def allgather_columns(c_local, N: int, group=None):
     for r, (n0, n1) in enumerate(shards):
         full[:, n0:n1] = blocks[r, :, : n1 - n0]
     return full
+
+
+def row_slice(M: int, world: int, rank: int) -> tuple[int, int, int]:
+    """(r0, r1, rows): the rows [r0, r1) of A that `rank` uploads from host
+    memory when every rank needs all of A, and the per-rank slot height
+    rows = ceil(M / world) of the all-gather (the last slots may be short
+    or empty; the gathered buffer has world * rows rows, of which the first
+    M are A)."""
+    if world < 1 or not (0 <= rank < world) or M < 0:
+        raise ValueError(f"bad row slice request M={M} world={world} rank={rank}")
+    rows = (M + world - 1) // world
+    return min(M, rank * rows), min(M, (rank + 1) * rows), rows
+
+
+def gpu_local_cpus(device: int):
+    """The host CPUs NVML reports as close to `device` (its NUMA node),
+    restricted to the CPUs this process may run on; None when unknown."""
+    try:
+        import pynvml
+        import torch
+
+        props = torch.cuda.get_device_properties(device)
+        bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+        pynvml.nvmlInit()
+        h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        words = pynvml.nvmlDeviceGetCpuAffinity(h, ((os.cpu_count() or 64) + 63) // 64)
+        cpus = {64 * i + b for i, w in enumerate(words) for b in range(64) if (int(w) >> b) & 1}
+        cpus &= os.sched_getaffinity(0)
+        return cpus or None
+    except Exception:
+        return None
+
+
+def bind_to_gpu_numa_node(device: int) -> list[int] | None:
+    """Run this process on the CPUs next to `device`, so that pinned host
+    buffers allocated afterwards sit in that NUMA node's memory and host <->
+    device copies do not cross the inter-socket link.  Returns the CPU list,
+    or None (nothing changed) when NVML cannot tell."""
+    cpus = gpu_local_cpus(device)
+    if cpus is None:
+        return None
+    os.sched_setaffinity(0, cpus)
+    return sorted(cpus)
+
+
+class ShardedHostGemm:
+    """One rank of an N-sharded GEMM with host-resident operands:
+    C_local = A . B_local^T, where every rank needs all of A (M x K) but holds
+    only its rows [r0, r1) of it in host memory (`row_slice`).
+
+    Each `run` copies this rank's rows of A and its B rows from host memory,
+    gathers the other ranks' rows of A over NVLink with one all-gather of
+    the process group (in place, in rank order), runs the GEMM on the device
+    and copies C_local back to host memory.  The host link therefore carries
+    A once per node instead of once per GPU.
+
+    Two sets of device buffers alternate between consecutive calls: a call
+    issued on another stream uploads while the previous call's GEMM and
+    copy-out still run; a set is reused only after the call two back has
+    finished with it.  `gemm_fn(A_full, B, C, stream)` runs the GEMM on
+    device tensors (A_full has world * rows rows, of which the first M are A)
+    and returns a status code (0 = OK).  With device "cpu" (tests on CPU
+    process groups) there are no streams or events."""
+
+    def __init__(self, M: int, N_local: int, K: int, gemm_fn, device, group=None):
+        import torch
+        import torch.distributed as dist
+
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.group = group
+        self.M, self.N_local, self.K = M, N_local, K
+        self.r0, self.r1, self.rows = row_slice(M, self.world, self.rank)
+        self.device = torch.device(device)
+        self.cuda = self.device.type == "cuda"
+        self._gemm = gemm_fn
+        self._sets = []
+        for _ in range(2):
+            self._sets.append({
+                "A": torch.empty(self.world * self.rows, K, dtype=torch.bfloat16, device=self.device),
+                "B": torch.empty(N_local, K, dtype=torch.bfloat16, device=self.device),
+                "C": torch.empty(M, N_local, dtype=torch.bfloat16, device=self.device),
+                "done": torch.cuda.Event() if self.cuda else None,
+                "used": False,
+            })
+        self._next = 0
+
+    def bytes_per_call(self) -> tuple[int, int]:
+        """(host -> device, device -> host) bytes one call moves on this rank."""
+        return 2 * ((self.r1 - self.r0) * self.K + self.N_local * self.K), 2 * self.M * self.N_local
+
+    def run(self, hA_rows, hB_local, hC_local, stream=None) -> None:
+        """hA_rows: host bf16 [r1 - r0, K] (this rank's rows of A); hB_local:
+        host bf16 [N_local, K]; hC_local: host bf16 [M, N_local] view (row
+        stride may exceed N_local).  Pinned host memory lets the copies run
+        asynchronously; completion is ordered on `stream` (default: the
+        current stream)."""
+        import torch
+        import torch.distributed as dist
+
+        if tuple(hA_rows.shape) != (self.r1 - self.r0, self.K):
+            raise ValueError(f"hA_rows must be rows [{self.r0}, {self.r1}) of A: got {tuple(hA_rows.shape)}")
+        if tuple(hB_local.shape) != (self.N_local, self.K) or tuple(hC_local.shape) != (self.M, self.N_local):
+            raise ValueError("hB_local / hC_local shape mismatch")
+        s = self._sets[self._next]
+        self._next ^= 1
+        if self.cuda:
+            stream = stream if stream is not None else torch.cuda.current_stream(self.device)
+            ctx = torch.cuda.stream(stream)
+        else:
+            ctx = contextlib.nullcontext()
+        with ctx:
+            if self.cuda and s["used"]:
+                stream.wait_event(s["done"])  # the call two back is done with this set
+            slot = s["A"][self.rank * self.rows:(self.rank + 1) * self.rows]
+            slot[: self.r1 - self.r0].copy_(hA_rows, non_blocking=True)
+            s["B"].copy_(hB_local, non_blocking=True)
+            if self.world > 1:
+                dist.all_gather_into_tensor(s["A"].view(-1), slot.reshape(-1), group=self.group)
+            rc = self._gemm(s["A"], s["B"], s["C"], stream)
+            if rc != 0:
+                raise RuntimeError(f"sharded host GEMM: status {rc}")
+            hC_local.copy_(s["C"], non_blocking=True)
+            if self.cuda:
+                s["done"].record(stream)
+        s["used"] = True
 
 
 def max_over_ranks(value: float, device=None, group=None) -> float:

@@ -16,10 +16,20 @@ no collective on the compute path.  For "square8192" each rank owns a fixed
 and "mlp" the global N is fixed and split (strong scaling).  --allgather adds
 a separately timed NCCL all-gather of the C shards.
 
+Every run also carries a "strong16384" block (skip with --no-strong): the
+16384^3 GEMM split along N over all ranks (strong scaling; at one GPU the
+whole 16384^3), its separately timed NCCL all-gather of C and the GEMM with
+the all-gather fused into its epilogue (checked bit for bit against a
+single-GPU GEMM first), and its end-to-end rate from host memory, where each
+rank uploads only its share of A's rows and gathers the rest over NVLink.
+
 --impl reference times the reference implementation of the path on the
 host CPU cores: the reference project has no CPU GEMM of its own, so this
 arm runs the C restatement of its arithmetic (oracle/, multithreaded fp32)
-on a bounded row sample of the same workload.
+on a bounded row sample of the same workload.  When the reference's own
+B200 kernel was built from its sources (oracle/_ref/libref_gemm.so) and a
+GPU is present, the line also carries "reference_kernel": that kernel timed
+on the same shape and operand distribution, exactly like `value`.
 """
 from __future__ import annotations
 
@@ -81,6 +91,9 @@ def parse_args(argv=None):
     p.add_argument("--no-cublas", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-strong", action="store_true", help="skip the strong16384 block")
+    p.add_argument("--no-numa-bind", action="store_true",
+                   help="do not move each rank onto the CPUs of its GPU's NUMA node")
     p.add_argument("--cpu-seconds", type=float, default=10.0,
                    help="target CPU time of the cpu_baseline sample")
     return p.parse_args(argv)
@@ -362,8 +375,88 @@ def cpu_baseline(w, seed: int, target_s: float):
             "seconds": dt, "ncpus": oracle.num_cpus(), "cpu_model": cpu_model()}
 
 
+def bench_config(args, w, world: int, rank: int = 0, library_arm: bool = False):
+    """The `config` object of the JSON line, identical for both arms of a run
+    (the reference arm computes it for the same --gpus N without a GPU)."""
+    M, Nl, K, _ = shard_shape(w, world, rank)
+    nw = w.get("weights", 1)
+    operand_bytes = (M * K + nw * Nl * K) * 2
+    flush = operand_bytes < 2 * L2_BYTES
+    cfg = {"workload": args.workload, "M": M, "N_per_gpu": Nl, "K": K,
+           "N_global": Nl * world if w["scaling"] == "weak" else w["N"],
+           "dist": w["dist"], "seed": args.seed,
+           "parallelism": f"N-sharded x{world}, A replicated, no collective",
+           "l2": ("operands %.0f MB > 2x L2 (126 MB): back-to-back steps, no flush"
+                  % (operand_bytes / 1e6)) if not flush else
+                 ("operands %.0f MB < 2x L2: 256 MB L2 flush before each step, "
+                  "per-step CUDA events" % (operand_bytes / 1e6))}
+    if nw > 1:
+        cfg["weights"] = (f"{nw} weight matrices B rotate, step i uses B[i mod {nw}]; CUDA events "
+                          "only around the whole run")
+        cfg["launch_overlap"] = None if library_arm else "B200GEMM_PDL_WEIGHTS_EARLY"
+    return cfg, flush
+
+
+def reference_kernel_leg(args, w, steps: int, warmup: int):
+    """The reference's own B200 kernel, runKernel1 (b200_kernels/matmul_1.cuh:
+    386-418), built from its sources into oracle/_ref/libref_gemm.so, on the
+    workload's per-GPU shape and operand distribution, timed exactly like
+    `value` (back-to-back launches, CUDA events, same L2 rule).  Its result
+    is checked against cuBLASLt first.  None when the library or a GPU is
+    missing, or the shape is outside what the reference supports (M, N
+    multiples of 256, K a multiple of 64)."""
+    lib_path = ROOT / "oracle" / "_ref" / "libref_gemm.so"
+    M, N, K = w["M"], w["N"], w["K"]
+    if w.get("weights", 1) > 1 or M % 256 or N % 256 or K % 64:
+        return None
+    if not lib_path.exists():
+        return {"unavailable": "oracle/_ref/libref_gemm.so not built (needs the reference sources at build time)"}
+    try:
+        import torch
+    except Exception:
+        return None
+    if not torch.cuda.is_available():
+        return None
+    import ctypes
+
+    from b200_gemm_b200 import data
+
+    lib = ctypes.CDLL(str(lib_path))
+    lib.ref_run_kernel1.restype = ctypes.c_int
+    lib.ref_run_kernel1.argtypes = [ctypes.c_int] * 3 + [ctypes.c_void_p] * 3
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    A, B = data.device_operands(M, N, K, w["dist"], seed=args.seed, device=dev)
+    C = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    a, b, c = A.data_ptr(), B.data_ptr(), C.data_ptr()
+
+    def step():
+        rc = lib.ref_run_kernel1(M, N, K, a, b, c)
+        if rc != 0:
+            raise RuntimeError(f"reference kernel launch: CUDA error {rc}")
+
+    step()
+    torch.backends.cuda.preferred_blas_library("cublaslt")
+    R = torch.matmul(A, B.t())
+    torch.cuda.synchronize()
+    ok = bool(((C.float() - R.float()).abs() <= 2.0 ** -7 * (R.float().abs() + 1.0)).all())
+    del R
+    for _ in range(max(3, warmup)):
+        step()
+    stream = torch.cuda.current_stream(dev)
+    flush = (M * K + N * K) * 2 < 2 * L2_BYTES
+    with ClockSampler(0) as clocks:
+        ms = time_steps(torch, step, steps, flush, stream, dev, torch.cuda.synchronize)
+    return {"value": 2.0 * M * N * K / (ms / 1e3 / steps) / 1e12, "unit": "TFLOPS",
+            "ms_per_launch": ms / steps, "steps": steps, "shape": [M, N, K],
+            "matches_cublaslt": ok, "clocks": clocks.summary(),
+            "how": "reference runKernel1 built from its sources (oracle/_ref/libref_gemm.so), one GPU, "
+                   "same operands and timing rule as `value` of the GPU arm"}
+
+
 def run_reference(args, w):
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return 0  # the CPU arm runs on rank 0 only
     from oracle import oracle
@@ -385,20 +478,24 @@ def run_reference(args, w):
     total = sum(times)
     flops = 2.0 * rows * N * K * args.steps
     value = flops / total / 1e12
+    config, _ = bench_config(args, w, max(1, args.gpus))
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOPS",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True,
-        "scaling": w["scaling"], "vs_baseline": None, "dtype": "f32 (bf16 inputs widened)",
-        "data": "synthetic", "config": {"workload": args.workload, "M": w["M"], "N": N, "K": K,
-                                         "dist": w["dist"], "rows_per_step": rows},
+        "scaling": w["scaling"] if world > 1 else "weak", "vs_baseline": None,
+        "dtype": "f32 (bf16 inputs widened)", "data": "synthetic", "config": config,
         "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": used, "kind": "port",
                          "sample": f"{rows} of {w['M']} rows of C per step (full N, K), "
                                    "C restatement of the reference arithmetic, fp32 accumulate; "
                                    "the rate extrapolates linearly in M to the whole workload",
+                         "rows_per_step": rows,
                          "ncpus": oracle.num_cpus(), "cpu_model": cpu_model()},
         "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    rk = reference_kernel_leg(args, w, max(3, args.steps), args.warmup)
+    if rk is not None:
+        line["reference_kernel"] = rk
     print(json.dumps(line), flush=True)
     return 0
 
@@ -418,6 +515,12 @@ def run_ours(args, w):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     distributed = world > 1
+    from b200_gemm_b200 import shard
+
+    # Pinned host buffers (e2e legs) go to the GPU's own NUMA node; the CPU
+    # baseline gets the whole machine back before it runs.
+    all_cpus = os.sched_getaffinity(0)
+    numa_cpus = None if args.no_numa_bind else shard.bind_to_gpu_numa_node(local)
     if distributed:
         import datetime
 
@@ -574,6 +677,11 @@ def run_ours(args, w):
         extra["e2e"] = e2e
 
     del A, B, C, Bs
+    # ------------------------------------ 16384^3 split over all ranks (strong)
+    if not args.no_strong and not library_arm:
+        torch.cuda.empty_cache()
+        extra["strong16384"] = run_strong16384(gemm, torch, dev, stream, args, barrier, distributed,
+                                               world, rank)
     info = gemm.device_info()
     result = None
     if rank == 0:
@@ -584,18 +692,7 @@ def run_ours(args, w):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
             "higher_is_better": True, "scaling": w["scaling"] if world > 1 else "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": args.workload, "M": M, "N_per_gpu": Nl, "K": K,
-                       "N_global": Nl * world if w["scaling"] == "weak" else w["N"],
-                       "dist": w["dist"], "seed": args.seed,
-                       "parallelism": f"N-sharded x{world}, A replicated, no collective",
-                       "l2": ("operands %.0f MB > 2x L2 (126 MB): back-to-back steps, no flush"
-                              % (operand_bytes / 1e6)) if not flush else
-                             ("operands %.0f MB < 2x L2: 256 MB L2 flush before each step, "
-                              "per-step CUDA events" % (operand_bytes / 1e6)),
-                       **({"weights": f"{nw} weight matrices B rotate, step i uses B[i mod {nw}]; CUDA events "
-                                      "only around the whole run",
-                           "launch_overlap": None if library_arm else "B200GEMM_PDL_WEIGHTS_EARLY"}
-                          if nw > 1 else {})},
+            "config": bench_config(args, w, world, rank, library_arm)[0],
             "gpu_launches": 0 if library_arm else args.steps,
             "launch": launch_shape(gemm, M, Nl, K, info, library_arm),
             "roofline": roofline(w, M, Nl, K, ms / args.steps, peaks, peak_kind, traffic),
@@ -615,7 +712,10 @@ def run_ours(args, w):
             result["tile_width"] = plan["tile_width"] if plan["kernel"] == "tiled" else None
             if plan["kernel"].startswith("small_m"):
                 result["small_m_split"] = plan["small_m_split"]
+        if numa_cpus is not None:
+            result["host_cpus"] = {"bound_to_gpu_numa_node": True, "cpus": len(numa_cpus)}
         if not args.no_cpu_baseline and not library_arm:
+            os.sched_setaffinity(0, all_cpus)
             result["cpu_baseline"] = cpu_baseline(w, args.seed, args.cpu_seconds)
     gemm.close()
     if distributed:
@@ -626,35 +726,22 @@ def run_ours(args, w):
     return 0
 
 
-def run_e2e(gemm, torch, dev, stream, M, Nl, K, A, B, args, barrier, distributed, world):
-    """Same metric through the public host-buffer entry point: each step hands
-    pinned host A and B to b200gemm_bf16_nt_host, which copies them in, runs
-    the GEMM and copies C back out to pinned host memory, pipelined by row
-    chunks on its own streams; the step completes on `stream`."""
-    hA = torch.empty(M, K, dtype=torch.bfloat16, pin_memory=True)
-    hB = torch.empty(Nl, K, dtype=torch.bfloat16, pin_memory=True)
-    hC = torch.empty(M, Nl, dtype=torch.bfloat16, pin_memory=True)
-    hA.copy_(A)
-    hB.copy_(B)
-
-    # Steps alternate between two streams, as independent requests would
-    # arrive, so one step's uploads overlap the previous step's last GEMM and
-    # copy-out (calls on one stream run one after the other).
+def time_e2e(torch, dev, stream, step, steps, barrier, distributed):
+    """Device ms for `steps` calls of step(i, stream_i), the calls alternating
+    between `stream` and a second stream, as independent requests would
+    arrive (calls on one stream run one after the other); CUDA events on
+    `stream`, which waits for the other stream before the end event; max
+    over ranks."""
     streams = [stream, torch.cuda.Stream(device=dev)]
-
-    def step(i):
-        gemm.bf16_nt_host(hA, hB, out=hC, stream=streams[i % 2])
-
-    steps = max(3, min(args.steps, 20))
     for i in range(3):
-        step(i)
+        step(i, streams[i % 2])
     streams[0].wait_stream(streams[1])
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     streams[1].wait_event(e0)
     for i in range(steps):
-        step(i)
+        step(i, streams[i % 2])
     streams[0].wait_stream(streams[1])
     e1.record(stream)
     barrier()
@@ -665,12 +752,180 @@ def run_e2e(gemm, torch, dev, stream, M, Nl, K, A, B, args, barrier, distributed
         t = torch.tensor([ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
+    return ms
+
+
+def host_e2e(gemm, torch, dev, stream, M, Nl, K, A, B, steps, barrier, distributed, world):
+    """One rank's end-to-end GEMM from pinned host memory, through the
+    library's public host-buffer paths:
+      * one GPU: b200gemm_bf16_nt_host (C-ABI) with host A, B and C, which
+        copies them in and out by row chunks overlapped with the GEMMs;
+      * N GPUs: shard.ShardedHostGemm, where each rank holds and uploads only
+        its 1/N of A's rows plus its own B rows, gathers the rest of A from
+        the other ranks over NVLink (one NCCL all-gather), runs the GEMM
+        through the C-ABI and copies its C columns out.
+    Returns (ms for `steps` calls, max over ranks; h2d bytes; d2h bytes) per
+    rank and call."""
+    from b200_gemm_b200 import _lib, shard
+
+    hB = torch.empty(Nl, K, dtype=torch.bfloat16, pin_memory=True)
+    hC = torch.empty(M, Nl, dtype=torch.bfloat16, pin_memory=True)
+    hB.copy_(B)
+    if world == 1:
+        hA = torch.empty(M, K, dtype=torch.bfloat16, pin_memory=True)
+        hA.copy_(A)
+
+        def step(i, s):
+            gemm.bf16_nt_host(hA, hB, out=hC, stream=s)
+
+        up, down = 2 * (M * K + Nl * K), 2 * M * Nl
+    else:
+        def gemm_fn(A_full, Bd, Cd, s):
+            return gemm.bf16_nt_ptr(M, Nl, K, A_full.data_ptr(), Bd.data_ptr(), Cd.data_ptr(), Nl,
+                                    int(s.cuda_stream))
+
+        hg = shard.ShardedHostGemm(M, Nl, K, gemm_fn, dev)
+        hA_rows = torch.empty(hg.r1 - hg.r0, K, dtype=torch.bfloat16, pin_memory=True)
+        hA_rows.copy_(A[hg.r0:hg.r1])
+
+        def step(i, s):
+            hg.run(hA_rows, hB, hC, s)
+
+        up, down = hg.bytes_per_call()
+    ms = time_e2e(torch, dev, stream, step, steps, barrier, distributed)
+    st, detail = gemm.last_device_status()
+    if st != _lib.OK:
+        raise RuntimeError(f"device status {st} {detail}")
+    return ms, up, down
+
+
+def run_e2e(gemm, torch, dev, stream, M, Nl, K, A, B, args, barrier, distributed, world):
+    """Same metric through the public host-buffer entry points (host_e2e)."""
+    steps = max(3, min(args.steps, 20))
+    ms, up, down = host_e2e(gemm, torch, dev, stream, M, Nl, K, A, B, steps, barrier, distributed, world)
     value = 2.0 * M * Nl * K * world / (ms / 1e3 / steps) / 1e12
-    return {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 2 * (M * K + Nl * K),
-            "d2h_bytes_per_step": 2 * M * Nl, "steps": steps,
-            "how": "pinned host A,B,C through b200gemm_bf16_nt_host (row-chunked; H2D, GEMM and D2H "
-                   "overlapped on three streams); steps alternate between two caller streams; CUDA "
-                   "events on the first, which waits for the second before the end event"}
+    how = ("pinned host A,B,C through b200gemm_bf16_nt_host (row-chunked; H2D, GEMM and D2H overlapped on "
+           "three streams)" if world == 1 else
+           "shard.ShardedHostGemm: each rank uploads its 1/N of A's rows and its B rows from pinned host "
+           "memory, one NCCL all-gather assembles A over NVLink, GEMM through the C-ABI, C columns copied "
+           "back to pinned host memory")
+    return {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": up * world,
+            "d2h_bytes_per_step": down * world, "per_rank_h2d_bytes": up, "per_rank_d2h_bytes": down,
+            "steps": steps,
+            "how": how + "; steps alternate between two caller streams; CUDA events on the first, which "
+                         "waits for the second before the end event; max over ranks"}
+
+
+def run_strong16384(gemm, torch, dev, stream, args, barrier, distributed, world, rank):
+    """The north-star scaling configuration: C = A . B^T at M = N = K = 16384
+    (N(0,1) operands), B and C column-sharded over all ranks, A replicated
+    (at one GPU the whole GEMM).  Times the GEMM (max over ranks, aggregate
+    TFLOPS), the NCCL all-gather of the C shards separately, the GEMM with
+    the all-gather fused into its epilogue (b200gemm_bf16_nt_allgather; first
+    checked bit for bit on every rank against a one-GPU 16384^3 GEMM), and
+    the end-to-end rate from pinned host memory (host_e2e)."""
+    import torch.distributed as dist
+
+    from b200_gemm_b200 import _lib, data, shard
+
+    M = N = K = 16384
+    n0, n1 = shard.column_shard(N, world, rank)
+    Nl = n1 - n0
+    flops = 2.0 * M * N * K
+    A, B_full = data.device_operands(M, N, K, "normal", seed=args.seed + 100, device=dev)
+    B = B_full[n0:n1].contiguous() if Nl != N else B_full
+    C = torch.empty(M, Nl, dtype=torch.bfloat16, device=dev)
+    sptr = int(stream.cuda_stream)
+    a, b, c = A.data_ptr(), B.data_ptr(), C.data_ptr()
+
+    def step():
+        rc = gemm.bf16_nt_ptr(M, Nl, K, a, b, c, Nl, sptr)
+        if rc != _lib.OK:
+            raise RuntimeError(_lib.strerror(rc))
+
+    def max_ms(ms):
+        if not distributed:
+            return ms
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    steps = max(5, min(args.steps, 20))
+    for _ in range(3):
+        step()
+    barrier()
+    ms = max_ms(time_steps(torch, step, steps, False, stream, dev, barrier))
+    plan = gemm.plan(M, Nl, K)
+    res = {"M": M, "N": N, "K": K, "N_per_gpu": Nl, "n_gpus": world, "dist": "normal",
+           "scaling": "strong", "steps": steps, "ms_per_step": ms / steps,
+           "value": flops / (ms / 1e3 / steps) / 1e12, "unit": "TFLOPS",
+           "tile_width": plan["tile_width"], "tail_split": plan["tail_split"],
+           "how": "B and C column-sharded (shard.column_shard), A replicated, no collective; back-to-back "
+                  "launches, CUDA events, max over ranks; value = 2*16384^3 / per-step time"}
+    reps = max(3, min(args.steps, 20))
+    if distributed:
+        gathered = torch.empty(world * M * Nl, dtype=torch.bfloat16, device=dev)
+        flat = C.view(-1)
+        for _ in range(3):
+            dist.all_gather_into_tensor(gathered, flat)
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            dist.all_gather_into_tensor(gathered, flat)
+        e1.record(stream)
+        barrier()
+        ag_ms = max_ms(e0.elapsed_time(e1) / reps)
+        nbytes = gathered.numel() * 2
+        res["allgather"] = {"ms": ag_ms, "bytes_out_per_rank": nbytes,
+                            "busbw_gbs": nbytes * (world - 1) / world / (ag_ms / 1e3) / 1e9,
+                            "gemm_plus_allgather_ms": ms / steps + ag_ms,
+                            "how": "NCCL all_gather_into_tensor of the C shards (shard-major), timed "
+                                   "separately from the GEMM, CUDA events, max over ranks"}
+        del gathered
+        fused = shard.FusedAllGather(gemm, M, N)
+        try:
+            fused.C.fill_(float("nan"))
+            barrier()
+            rc = fused.run(A, B, sptr)
+            barrier()
+            full = gemm.bf16_nt(A, B_full)
+            torch.cuda.synchronize()
+            same = torch.tensor([1 if rc == _lib.OK and torch.equal(
+                fused.view().view(torch.int16), full.view(torch.int16)) else 0], device=dev)
+            del full
+            dist.all_reduce(same, op=dist.ReduceOp.MIN)
+            bit_exact = bool(same.item())
+            fstep = lambda: fused.run(A, B, sptr)  # noqa: E731
+            for _ in range(3):
+                fstep()
+            barrier()
+            fms = max_ms(time_steps(torch, fstep, reps, False, stream, dev, barrier)) / reps
+            res["fused_allgather"] = {
+                "ms": fms, "bit_exact": bit_exact, "tflops_aggregate": flops / (fms / 1e3) / 1e12,
+                "vs_gemm_plus_allgather": (ms / steps + ag_ms) / fms,
+                "how": "b200gemm_bf16_nt_allgather: the epilogue writes each C chunk into every rank's "
+                       "full-width C over NVLink (IPC-mapped peer stores); bit_exact: every rank's "
+                       "gathered C equals its own one-GPU 16384^3 GEMM, bit for bit"}
+        finally:
+            barrier()
+            fused.close()
+            del fused
+    st, detail = gemm.last_device_status()
+    if st != _lib.OK:
+        raise RuntimeError(f"device status {st} {detail}")
+    if not args.no_e2e:
+        e_steps = max(3, min(args.steps, 10))
+        del C
+        ems, up, down = host_e2e(gemm, torch, dev, stream, M, Nl, K, A, B, e_steps, barrier, distributed,
+                                 world)
+        res["e2e"] = {"value": flops / (ems / 1e3 / e_steps) / 1e12, "unit": "TFLOPS", "steps": e_steps,
+                      "h2d_bytes_per_step": up * world, "d2h_bytes_per_step": down * world,
+                      "per_rank_h2d_bytes": up, "per_rank_d2h_bytes": down,
+                      "how": "host_e2e: one GPU b200gemm_bf16_nt_host; N GPUs shard.ShardedHostGemm (each "
+                             "rank uploads 1/N of A's rows and its B rows, NCCL all-gather of A over "
+                             "NVLink, GEMM, C columns back to host); max over ranks"}
+    return res
 
 
 def main(argv=None):

@@ -267,8 +267,8 @@ int b200gemm_schedule_host(unsigned int tiles_m, unsigned int tiles_n, int order
  *    chosen per shape; e.g. 32768 x 32768 fits); larger problems return
  *    B200GEMM_ERR_TOO_LARGE before any GPU work.
  *  - The first call on a device sets up that device (looks up the array's
- *    device address, sets kernel attributes); make it before any stream
- *    capture.
+ *    device address, sets kernel attributes, loads every kernel this entry
+ *    point launches); make it before any stream capture.
  *  - All calls share the array, which keeps the last call's contents; each
  *    call clears the status words and rewrites the schedule on `stream`, so
  *    calls that overlap on the GPU (different streams, not ordered) race.
