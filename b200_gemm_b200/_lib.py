@@ -54,6 +54,8 @@ SIGNATURES = {
                                            ctypes.POINTER(Epilogue), _vp]),
     "b200gemm_bf16_nt_allgather": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp, _vp, _vp, _c_int,
                                             ctypes.POINTER(_vp), _c_int, _vp]),
+    "b200gemm_bf16_nt_allgather_multicast": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp, _vp, _vp, _c_int,
+                                                      _vp, _vp]),
     "b200gemm_ipc_get_handle": (_c_int, [_vp, _vp, ctypes.POINTER(_c_ull)]),
     "b200gemm_ipc_open": (_c_int, [_vp, ctypes.POINTER(_vp)]),
     "b200gemm_ipc_close": (_c_int, [_vp]),

@@ -27,7 +27,7 @@ namespace b200gemm {
 #define B200GEMM_STAGES_N512 3
 #endif
 #ifndef B200GEMM_EPIWARPS_N512
-#define B200GEMM_EPIWARPS_N512 16
+#define B200GEMM_EPIWARPS_N512 8
 #endif
 // L2 sector promotion of every tensor map's loads (CUtensorMapL2promotion:
 // 0 none, 1 64 B, 2 128 B, 3 256 B).
@@ -41,8 +41,10 @@ namespace b200gemm {
 #define B200GEMM_DEFAULT_BAND 16
 #endif
 using CfgN256 = GemmCfg<B200GEMM_STAGES_N256, 1>;  // 256 x 256 tiles, overlapped epilogue
-// 256 x 512 tiles, shared A stage; 16 epilogue warps drain the single
-// 512-column accumulator (3 stages leave room for their staging buffers).
+// 256 x 512 tiles, shared A stage; 8 epilogue warps drain the single
+// 512-column accumulator, each reading its 8 chunks into 4 staging buffers
+// and registers before any store (3 stages leave room for the buffers; 8
+// warps leave 160+ registers per thread, so nothing spills).
 using CfgN512 = GemmCfg<B200GEMM_STAGES_N512, 2, 256, false, B200GEMM_EPIWARPS_N512>;
 // The same tiles, launched only when a short last wave runs as 256-column halves.
 using CfgN512H = GemmCfg<B200GEMM_STAGES_N512, 2, 256, false, B200GEMM_EPIWARPS_N512, true>;
@@ -942,7 +944,7 @@ extern "C" int b200gemm_set_pdl(b200gemm_t h, int mode) {
 namespace {
 int gemm_device(b200gemm_t h, int M, int N, int K, const void* A, const void* B, void* C, int ldc,
                 void* stream_ptr, bool allow_small_m, int npeers = 0,
-                void* const* peers = nullptr, const b200gemm_epilogue* epi = nullptr);
+                void* const* peers = nullptr, const b200gemm_epilogue* epi = nullptr, void* mc_c = nullptr);
 }  // namespace
 
 extern "C" int b200gemm_bf16_nt(b200gemm_t h, int M, int N, int K, const void* A, const void* B,
@@ -966,7 +968,18 @@ extern "C" int b200gemm_bf16_nt_allgather(b200gemm_t h, int M, int N, int K, con
     if ((reinterpret_cast<uintptr_t>(peer_C[i]) & 15u) != 0) return B200GEMM_ERR_UNSUPPORTED;
   }
   if ((N % 8) != 0) return B200GEMM_ERR_UNSUPPORTED;  // peer rows are copied in 16-byte pieces
+  if (K == 0 && M > 0 && N > 0) return B200GEMM_ERR_UNSUPPORTED;  // the peers' blocks would stay unwritten
   return gemm_device(h, M, N, K, A, B, C, ldc, stream_ptr, /*allow_small_m=*/false, npeers, peer_C);
+}
+
+extern "C" int b200gemm_bf16_nt_allgather_multicast(b200gemm_t h, int M, int N, int K, const void* A,
+                                                    const void* B, void* C, int ldc, void* mc_C,
+                                                    void* stream_ptr) {
+  if (mc_C == nullptr) return B200GEMM_ERR_INVALID_ARG;
+  if ((reinterpret_cast<uintptr_t>(mc_C) & 15u) != 0 || (N % 8) != 0) return B200GEMM_ERR_UNSUPPORTED;
+  if (K == 0 && M > 0 && N > 0) return B200GEMM_ERR_UNSUPPORTED;  // every rank's block would stay unwritten
+  return gemm_device(h, M, N, K, A, B, C, ldc, stream_ptr, /*allow_small_m=*/false, 0, nullptr, nullptr,
+                     mc_C);
 }
 
 extern "C" int b200gemm_ipc_get_handle(const void* dev_ptr, void* handle_out,
@@ -1020,7 +1033,7 @@ namespace {
 // element gets).
 int gemm_device(b200gemm_t h, int M, int N, int K, const void* A, const void* B, void* C, int ldc,
                 void* stream_ptr, bool allow_small_m, int npeers, void* const* peers,
-                const b200gemm_epilogue* epi) {
+                const b200gemm_epilogue* epi, void* mc_c) {
   if (h == nullptr || M < 0 || N < 0 || K < 0) return B200GEMM_ERR_INVALID_ARG;
   const bool fused = epi != nullptr;
   const int c_type = fused ? epi->out_type : B200GEMM_OUT_BF16;
@@ -1060,7 +1073,8 @@ int gemm_device(b200gemm_t h, int M, int N, int K, const void* A, const void* B,
   unsigned long long decode_timeout;
   int pdl;
   // Their C stores clip N in 16-byte units: e4m3 output needs N % 16 == 0.
-  const bool smallm_ok = allow_small_m && npeers == 0 && (c_type != B200GEMM_OUT_E4M3 || (N % 16) == 0);
+  const bool smallm_ok = allow_small_m && npeers == 0 && mc_c == nullptr &&
+                         (c_type != B200GEMM_OUT_E4M3 || (N % 16) == 0);
   {
     std::lock_guard<std::mutex> lock(h->mu);
     if (smallm_ok && h->small_m != 0) sm = smallm_plan(h, M, N, K);
@@ -1100,9 +1114,10 @@ int gemm_device(b200gemm_t h, int M, int N, int K, const void* A, const void* B,
   p.npeers = npeers;
   for (int i = 0; i < GemmParams::kMaxPeers; ++i)
     p.peer_c[i] = i < npeers ? static_cast<uint8_t*>(peers[i]) : nullptr;
+  p.mc_c = static_cast<uint8_t*>(mc_c);
   // Launch overlap (no B-first variant here: the tile table comes first);
-  // the all-gather form keeps plain stream order.
-  p.pdl = (pdl != kPdlOff && npeers == 0) ? kPdlOn : kPdlOff;
+  // the all-gather forms keep plain stream order.
+  p.pdl = (pdl != kPdlOff && npeers == 0 && mc_c == nullptr) ? kPdlOn : kPdlOff;
 
   p.epi_flags = 0;
   p.act = B200GEMM_ACT_NONE;

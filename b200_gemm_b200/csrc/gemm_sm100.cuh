@@ -9,21 +9,25 @@
 //   * the smem ring is initialised once and runs across tiles (the
 //     reference re-initialises every barrier and cluster-syncs per tile,
 //     matmul_1.cuh:373-374);
-//   * two TMEM accumulators (2 x 256 fp32 columns) let the MMA warp start
-//     tile i+1 while four dedicated epilogue warps drain tile i;
+//   * 256-column tiles: two TMEM accumulators (2 x 256 fp32 columns) let the
+//     MMA warp start tile i+1 while four dedicated epilogue warps drain tile
+//     i; 256 x 512 tiles (two MMAs per K step sharing the A stage) fill TMEM
+//     with one accumulator, which 8 epilogue warps read out completely
+//     (into staging buffers and registers) before any store, so the next
+//     tile's MMAs wait only for the TMEM reads;
 //   * the epilogue reads 32 columns per tcgen05.ld, converts to bf16 (RNE),
-//     writes 128B-swizzled staging buffers (bank-conflict free) and streams
-//     them out with per-warp TMA stores, double-buffered;
+//     writes 64B-swizzled staging buffers (bank-conflict free) and streams
+//     them out with per-warp TMA stores;
 //   * ragged M, N and K (K % 8 == 0) are handled by TMA bounds (zero fill on
 //     loads, clipping on stores) instead of requiring multiples of 256/64;
 //     the one chunk that ends inside a 16-byte group when N % 8 != 0 is
 //     stored element by element;
 //   * every wait is bounded (see ptx_sm100.cuh).
 //
-// Warp roles (192 threads per CTA, one CTA per SM, clusters of 2 CTAs):
+// Warp roles (64 + 32 x EW threads per CTA, one CTA per SM, clusters of 2):
 //   warp 0      TMA producer (one lane), both CTAs
 //   warp 1      MMA issuer (one lane), leader CTA only; TMEM allocator
-//   warps 2..5  epilogue; warp w reads TMEM lanes 32*(w%4) .. +31
+//   warps 2..   EW epilogue warps; warp w reads TMEM lanes 32*(w%4) .. +31
 #pragma once
 
 #include <cstdint>
@@ -40,14 +44,9 @@
 #ifndef B200GEMM_L2_POLICY_B
 #define B200GEMM_L2_POLICY_B 1
 #endif
+// Staging buffers per epilogue warp of the plain 256 x 512 instances.
 #ifndef B200GEMM_CBUFS_N512
-#define B200GEMM_CBUFS_N512 2
-#endif
-// 256 x 512 tiles: chunks per epilogue warp held in registers (packed bf16)
-// between the TMEM read and the store, so the accumulator is released after
-// fewer store chains.
-#ifndef B200GEMM_HELD_N512
-#define B200GEMM_HELD_N512 3
+#define B200GEMM_CBUFS_N512 4
 #endif
 
 
@@ -88,6 +87,12 @@ struct GemmParams {
   static constexpr int kMaxPeers = 7;
   int npeers;
   uint8_t* peer_c[kMaxPeers];
+  // Fused all-gather through NVLink multicast: the multicast address of
+  // this rank's first column of C (same pitch ldc), or null.  Every staged
+  // chunk is written once with multimem.st; NVSwitch delivers it to every
+  // GPU of the multicast object, this one included, so the chunk is not
+  // also TMA-stored locally.
+  uint8_t* mc_c;
   // Split of the last, partial wave: work units [0, tail_start) are whole
   // tiles (tiles[u]); unit tail_start + r * tail_split + s is K slice s (of
   // tail_kb K blocks) of tile tiles[tail_start + r].  A K slice writes its
@@ -170,7 +175,7 @@ __device__ __forceinline__ WorkUnit unit_at(const GemmParams& p, uint32_t u) {
 //           the MMA of tile i+1 overlaps the epilogue of tile i.
 //   NB = 2: a pair computes 256 x 512 tiles as two N = 256 MMAs per K step
 //           that share the A stage: 25% fewer operand bytes into each SM per
-//           flop; the single 512-column accumulator is drained by 8 warps.
+//           flop; the single 512-column accumulator is drained by EW warps.
 //   MN (NB = 1 only): columns of one MMA and of the tile, a multiple of 32
 //           up to 256 (e.g. 224 = 1792 / 8 for an N-sharded MLP projection),
 //           so the tile width can divide N and fill the last wave.
@@ -207,19 +212,23 @@ struct GemmCfg {
   static constexpr int kWarpChunks = kColsPerWarp / kCBoxCols;
   static_assert(EW % 4 == 0 && kColsPerWarp % kCBoxCols == 0 && kWarpChunks >= 1, "epilogue warps");
   // K-split tail units (fp32 partials + reduction) are compiled into the
-  // plain instances with at most 8 epilogue warps (more warps leave too few
-  // registers per thread for the reduction); the host splits no other.
-  static constexpr bool kTailSplit = !EPI && EW <= 8;
-  // Plain instances with one accumulator: the last kHeldChunks chunks of
-  // each warp are read from TMEM into registers (16 per chunk) after the
-  // others went through the store chain; TMEM is released before those are
-  // stored.
-  static constexpr int kHeldChunks = (!EPI && NB == 2) ? (B200GEMM_HELD_N512 < kWarpChunks ? B200GEMM_HELD_N512 : kWarpChunks) : 0;
+  // plain 256-column-MMA-block instances with one column block (in the
+  // 512-wide instance the split only tied the narrower tiles and cost
+  // registers); the host splits no other.
+  static constexpr bool kTailSplit = !EPI && NB == 1 && EW <= 8;
   static constexpr int kThreads = 64 + 32 * kEpiWarps;
   // Staging buffers per epilogue warp: a chunk's buffer is free once the
   // TMA store issued kCBufs chunks earlier has read it (about a microsecond),
   // so more buffers let a warp drain its accumulator faster.
-  static constexpr int kCBufs = NB == 2 ? B200GEMM_CBUFS_N512 : 2;
+  static constexpr int kCBufs = (NB == 2 && !EPI) ? B200GEMM_CBUFS_N512 : 2;
+  // Plain instances with one accumulator: every epilogue warp reads all its
+  // chunks from TMEM before any TMA store, the first kCBufs into its staging
+  // buffers and the rest into registers, so the accumulator is released
+  // after the TMEM reads alone (epilogue of gemm_bf16_nt_sm100).  Loads go
+  // in pairs.
+  static constexpr int kHeldChunks = kWarpChunks - kCBufs;
+  static constexpr bool kStagedDrain =
+      !EPI && NB == 2 && kCBufs % 2 == 0 && kHeldChunks > 0 && kHeldChunks % 2 == 0;
   static constexpr int kStageBytesB = kBlockBytesB * NB;
   static constexpr uint32_t kTxBytes = 2 * (kStageBytesA + kStageBytesB);  // both CTAs
   // shared memory layout (offsets from a 1024-byte aligned base)
@@ -265,6 +274,71 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
 // distinct banks) and a TMA store.  TMA clips the innermost dimension in
 // 16-byte units, so the chunk that ends inside a 16-byte group (N not a
 // multiple of 16 / ESIZE) is written with per-element predicated stores.
+// The 16 words of one lane (one row of a 32 x 64-byte chunk) into staging
+// buffer `buf`, 64-byte swizzled (see store_c_chunk).
+__device__ __forceinline__ void stage_chunk_row(uint32_t buf, uint32_t lane, const uint32_t (&w)[16]) {
+  const uint32_t rowaddr = buf + lane * 64u;
+  const uint32_t sw = (lane >> 1) & 3u;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    ptx::st_shared_v4(rowaddr + ((static_cast<uint32_t>(j) ^ sw) << 4), w[4 * j], w[4 * j + 1], w[4 * j + 2],
+                      w[4 * j + 3]);
+  }
+}
+
+// The same from 32 fp32 accumulators, rounded to bf16 (RNE) pairwise as
+// they are written, so no packed copy of the chunk is held.
+__device__ __forceinline__ void stage_chunk_row_f32(uint32_t buf, uint32_t lane, const uint32_t (&v)[32]) {
+  const uint32_t rowaddr = buf + lane * 64u;
+  const uint32_t sw = (lane >> 1) & 3u;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    ptx::st_shared_v4(rowaddr + ((static_cast<uint32_t>(j) ^ sw) << 4), ptx::pack_bf16x2(v[8 * j], v[8 * j + 1]),
+                      ptx::pack_bf16x2(v[8 * j + 2], v[8 * j + 3]), ptx::pack_bf16x2(v[8 * j + 4], v[8 * j + 5]),
+                      ptx::pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
+  }
+}
+
+// Fused all-gather: copy a staged chunk (rows row.., columns col.. of this
+// rank's block) to every peer's C over NVLink: 32 rows x 64 B = 128
+// segments of 16 B; four consecutive lanes write one row's 64 B.  The
+// chunk must be staged and the warp synchronised.
+template <int ESIZE>
+__device__ __forceinline__ void copy_chunk_to_peers(uint32_t buf, int col, int row, uint32_t lane,
+                                                    const GemmParams& p) {
+  constexpr int kGroup = 16 / ESIZE;
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const uint32_t seg = static_cast<uint32_t>(it) * 32u + lane;
+    const uint32_t r = seg >> 2, q = seg & 3u;
+    uint32_t x0, x1, x2, x3;
+    ptx::ld_shared_v4(buf + r * 64u + ((q ^ ((r >> 1) & 3u)) << 4), x0, x1, x2, x3);
+    const int grow = row + static_cast<int>(r), gcol = col + static_cast<int>(q) * kGroup;
+    if (grow < p.M && gcol < p.N) {
+      const long long off = (static_cast<long long>(grow) * p.ldc + gcol) * ESIZE;
+      for (int i = 0; i < p.npeers; ++i) ptx::st_global_v4(p.peer_c[i] + off, x0, x1, x2, x3);
+    }
+  }
+}
+
+// Fused all-gather through NVLink multicast: write a staged chunk once to
+// the multicast address, same segment order as copy_chunk_to_peers.
+template <int ESIZE>
+__device__ __forceinline__ void copy_chunk_to_multicast(uint32_t buf, int col, int row, uint32_t lane,
+                                                        const GemmParams& p) {
+  constexpr int kGroup = 16 / ESIZE;
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const uint32_t seg = static_cast<uint32_t>(it) * 32u + lane;
+    const uint32_t r = seg >> 2, q = seg & 3u;
+    uint32_t x0, x1, x2, x3;
+    ptx::ld_shared_v4(buf + r * 64u + ((q ^ ((r >> 1) & 3u)) << 4), x0, x1, x2, x3);
+    const int grow = row + static_cast<int>(r), gcol = col + static_cast<int>(q) * kGroup;
+    if (grow < p.M && gcol < p.N)
+      ptx::multimem_st_v4(p.mc_c + (static_cast<long long>(grow) * p.ldc + gcol) * ESIZE, x0, x1, x2, x3);
+  }
+}
+
 template <class Cfg, int ESIZE = 2>
 __device__ __forceinline__ void store_c_chunk(const uint32_t (&w)[16], int col, int row,
                                               uint32_t lane, uint32_t cstage0, uint32_t& cbuf,
@@ -297,34 +371,19 @@ __device__ __forceinline__ void store_c_chunk(const uint32_t (&w)[16], int col, 
     // The TMA store that last read this buffer (two chunks ago) must be done.
     if (lane == 0) ptx::bulk_wait_group_read<Cfg::kCBufs - 1>();
     __syncwarp();
-    const uint32_t rowaddr = buf + lane * 64u;
-    const uint32_t sw = (lane >> 1) & 3u;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      ptx::st_shared_v4(rowaddr + ((static_cast<uint32_t>(j) ^ sw) << 4), w[4 * j], w[4 * j + 1],
-                        w[4 * j + 2], w[4 * j + 3]);
-    }
-    ptx::fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == 0) {
-      ptx::tma_store_2d(&map_c, buf, col, row);
-      ptx::bulk_commit_group();
-    }
-    if (p.npeers > 0) {
-      // Copy the staged chunk to every peer's C over NVLink: 32 rows x 64 B =
-      // 128 segments of 16 B; four consecutive lanes write one row's 64 B.
-#pragma unroll
-      for (int it = 0; it < 4; ++it) {
-        const uint32_t seg = static_cast<uint32_t>(it) * 32u + lane;
-        const uint32_t r = seg >> 2, q = seg & 3u;
-        uint32_t x0, x1, x2, x3;
-        ptx::ld_shared_v4(buf + r * 64u + ((q ^ ((r >> 1) & 3u)) << 4), x0, x1, x2, x3);
-        const int grow = row + static_cast<int>(r), gcol = col + static_cast<int>(q) * kGroup;
-        if (grow < p.M && gcol < p.N) {
-          const long long off = (static_cast<long long>(grow) * p.ldc + gcol) * ESIZE;
-          for (int i = 0; i < p.npeers; ++i) ptx::st_global_v4(p.peer_c[i] + off, x0, x1, x2, x3);
-        }
+    stage_chunk_row(buf, lane, w);
+    if (p.mc_c != nullptr) {
+      __syncwarp();
+      copy_chunk_to_multicast<ESIZE>(buf, col, row, lane, p);
+      __syncwarp();  // every lane has read the buffer before it is reused
+    } else {
+      ptx::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        ptx::tma_store_2d(&map_c, buf, col, row);
+        ptx::bulk_commit_group();
       }
+      if (p.npeers > 0) copy_chunk_to_peers<ESIZE>(buf, col, row, lane, p);
     }
     if (++cbuf == Cfg::kCBufs) cbuf = 0;
   }
@@ -929,33 +988,84 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
             chunk(c, res_w, res_b);
             if (c + 1 < Cfg::kWarpChunks) chunk(c + 1, res_b, res_w);
           }
-        } else if constexpr (Cfg::kHeldChunks > 0) {
-          constexpr int kFirst = Cfg::kWarpChunks - Cfg::kHeldChunks;
+        } else if constexpr (Cfg::kStagedDrain) {
+          // One accumulator for the whole tile: the next tile's MMAs wait
+          // until every warp has read its part, and those reads are bound by
+          // the SM's TMEM read rate (about 1.1 us for 256 KB).  So a warp
+          // reads all its chunks before any store, two loads in flight at a
+          // time: the first kCBufs go to its staging buffers, the others stay
+          // in registers as packed bf16; then it releases the accumulator and
+          // issues the TMA stores.  A slice that reaches past M or N takes the
+          // per-chunk path below.
+          constexpr int kStaged = Cfg::kCBufs, kHeld = Cfg::kHeldChunks;
+          const bool whole = row < p.M && col0 + Cfg::kColsPerWarp <= p.N;
+          if (whole) {
+            if (lane == 0) ptx::bulk_wait_group_read<0>();  // the previous tile's stores have read every buffer
+            __syncwarp();
+#pragma unroll
+            for (int c = 0; c < kStaged; c += 2) {
+              uint32_t v0[32], v1[32];
+              ptx::tmem_ld_32x32b_x32(t_row + c * kCBoxCols, v0);
+              ptx::tmem_ld_32x32b_x32(t_row + (c + 1) * kCBoxCols, v1);
+              ptx::tmem_wait_ld();
+              ptx::reg_fence32(v0);
+              ptx::reg_fence32(v1);
+              stage_chunk_row_f32(cstage0 + c * kCStageBytes, lane, v0);
+              stage_chunk_row_f32(cstage0 + (c + 1) * kCStageBytes, lane, v1);
+            }
+            uint32_t pk[kHeld][16];
+#pragma unroll
+            for (int h = 0; h < kHeld; h += 2) {
+              uint32_t v0[32], v1[32];
+              ptx::tmem_ld_32x32b_x32(t_row + (kStaged + h) * kCBoxCols, v0);
+              ptx::tmem_ld_32x32b_x32(t_row + (kStaged + h + 1) * kCBoxCols, v1);
+              ptx::tmem_wait_ld();
+              ptx::reg_fence32(v0);
+              ptx::reg_fence32(v1);
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                pk[h][i] = ptx::pack_bf16x2(v0[2 * i], v0[2 * i + 1]);
+                pk[h + 1][i] = ptx::pack_bf16x2(v1[2 * i], v1[2 * i + 1]);
+              }
+            }
+            // Every TMEM read of this warp is done: release the accumulator.
+            ptx::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive_cluster(tempty_leader0 + 8 * acc);
+            if (p.mc_c != nullptr) {
+              __syncwarp();
 #pragma unroll 1
-          for (int c = 0; c < kFirst; ++c) {
-            uint32_t v[32];
-            ptx::tmem_ld_32x32b_x32(t_row + c * kCBoxCols, v);
-            ptx::tmem_wait_ld();
-            ptx::reg_fence32(v);
-            store_bf16(c, v);
+              for (int c = 0; c < kStaged; ++c)
+                copy_chunk_to_multicast<2>(cstage0 + c * kCStageBytes, col0 + c * kCBoxCols, row, lane, p);
+              __syncwarp();
+            } else {
+              ptx::fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+#pragma unroll
+                for (int c = 0; c < kStaged; ++c) {
+                  ptx::tma_store_2d(&map_c, cstage0 + c * kCStageBytes, col0 + c * kCBoxCols, row);
+                  ptx::bulk_commit_group();
+                }
+              }
+              if (p.npeers > 0) {
+#pragma unroll 1
+                for (int c = 0; c < kStaged; ++c)
+                  copy_chunk_to_peers<2>(cstage0 + c * kCStageBytes, col0 + c * kCBoxCols, row, lane, p);
+              }
+            }
+            cbuf = 0;  // held chunk h reuses buffer h % kCBufs once the store before it there has read it
+#pragma unroll
+            for (int h = 0; h < kHeld; ++h)
+              store_c_chunk<Cfg>(pk[h], col0 + (kStaged + h) * kCBoxCols, row, lane, cstage0, cbuf, map_c, p);
+          } else {
+#pragma unroll 1
+            for (int c = 0; c < Cfg::kWarpChunks; ++c) {
+              uint32_t v[32];
+              tmem_chunk(c, v);  // releases the accumulator after the last chunk's read
+              store_bf16(c, v);
+            }
           }
-          uint32_t pk[Cfg::kHeldChunks][16];
-#pragma unroll
-          for (int h = 0; h < Cfg::kHeldChunks; ++h) {
-            uint32_t v[32];
-            ptx::tmem_ld_32x32b_x32(t_row + (kFirst + h) * kCBoxCols, v);
-            ptx::tmem_wait_ld();
-            ptx::reg_fence32(v);
-#pragma unroll
-            for (int i = 0; i < 16; ++i) pk[h][i] = ptx::pack_bf16x2(v[2 * i], v[2 * i + 1]);
-          }
-          // Every TMEM read of this warp is done: release the accumulator.
-          ptx::tc_fence_before();
-          __syncwarp();
-          if (lane == 0) ptx::mbar_arrive_cluster(tempty_leader0 + 8 * acc);
-#pragma unroll
-          for (int h = 0; h < Cfg::kHeldChunks; ++h)
-            store_c_chunk<Cfg>(pk[h], col0 + (kFirst + h) * kCBoxCols, row, lane, cstage0, cbuf, map_c, p);
         } else {
 #pragma unroll 1
           for (int c = 0; c < Cfg::kWarpChunks; ++c) {
@@ -1059,7 +1169,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
       }
     }
     if (lane == 0) ptx::bulk_wait_group_read<0>();  // staging reusable; the stores land before the kernel completes
-    if (p.npeers > 0) __threadfence_system();  // peer copies visible before the kernel ends
+    if (p.npeers > 0 || p.mc_c != nullptr) __threadfence_system();  // peer copies visible before the kernel ends
     __syncwarp();
   }
 

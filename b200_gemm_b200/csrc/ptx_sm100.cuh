@@ -438,6 +438,14 @@ __device__ __forceinline__ void st_global_v4(void* ptr, uint32_t a, uint32_t b, 
                : "memory");
 }
 
+// 16-byte store through an NVLink multicast (NVLS) mapping: NVSwitch
+// replicates it into the memory of every GPU bound to the multicast object.
+// The words are stored as they are (a store does not interpret them).
+__device__ __forceinline__ void multimem_st_v4(void* mc_ptr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("multimem.st.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc_ptr), "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
+
 // 16-byte load cached in L2 only (data written by other SMs in this launch).
 __device__ __forceinline__ void ld_global_cg_v4(const void* ptr, uint32_t& a, uint32_t& b, uint32_t& c,
                                                 uint32_t& d) {

@@ -58,6 +58,76 @@ def allgather_columns(c_local, N: int, group=None):
     return full
 
 
+class MulticastAllGather:
+    """Full-width C on every rank, filled by one fused GEMM + all-gather that
+    writes through an NVLink multicast (NVLS) mapping.
+
+    C is allocated from torch's symmetric memory and rendezvoused over the
+    process group (plumbing only: torch creates the multicast object, binds
+    every rank's C to it and exchanges the handles).  `run` calls
+    b200gemm_bf16_nt_allgather_multicast, whose epilogue writes each finished
+    chunk of this rank's column block once, with multimem.st, to the
+    multicast address; NVSwitch replicates it into every rank's C.  After
+    `run` the caller's stream holds the completed writes; a barrier among
+    the ranks makes all blocks visible everywhere.
+
+    Raises RuntimeError when the node offers no multicast mapping.  `close`
+    is collective (a barrier, then the buffer is released on every rank):
+    no rank may drop its buffer while others can still write to it.
+    """
+
+    def __init__(self, gemm, M: int, N: int, group=None):
+        import torch
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+
+        from . import _lib
+
+        self._lib = _lib.load()
+        self.gemm = gemm
+        self.group = group if group is not None else dist.group.WORLD
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.M, self.N = M, N
+        self.pitch = 8 * ((N + 7) // 8)
+        self.n0, self.n1 = column_shard(N, self.world, self.rank)
+        if (self.n1 - self.n0) % 8 != 0:
+            raise ValueError("every column shard must be a multiple of 8 columns")
+        dev = torch.device("cuda", gemm.device)
+        self.C = symm_mem.empty(M, self.pitch, dtype=torch.bfloat16, device=dev)
+        self._hdl = symm_mem.rendezvous(self.C, self.group)
+        mc = int(self._hdl.multicast_ptr or 0)
+        if mc == 0:
+            self.close()
+            raise RuntimeError("no NVLink multicast mapping on this node (symmetric memory reports none)")
+        # The multicast range mirrors the rank's buffer; C sits at the same
+        # offset in both.
+        self.mc_base = mc + (self.C.data_ptr() - int(self._hdl.buffer_ptrs[self.rank]))
+
+    def run(self, A, B_local, stream_ptr: int) -> int:
+        """C[:, n0:n1] = A @ B_local^T on every rank's C; returns the status."""
+        off = self.n0 * 2
+        K = A.shape[1]
+        return self._lib.b200gemm_bf16_nt_allgather_multicast(
+            self.gemm._h, self.M, self.n1 - self.n0, K, A.data_ptr(), B_local.data_ptr(),
+            self.C.data_ptr() + off, self.pitch, self.mc_base + off, stream_ptr)
+
+    def view(self):
+        return self.C[:, : self.N]
+
+    def close(self) -> None:
+        import torch
+        import torch.distributed as dist
+
+        if getattr(self, "C", None) is None:
+            return
+        torch.cuda.synchronize(self.C.device)
+        dist.barrier(group=self.group)
+        self._hdl = None
+        self.C = None
+        torch.cuda.synchronize()
+
+
 def row_slice(M: int, world: int, rank: int) -> tuple[int, int, int]:
     """(r0, r1, rows): the rows [r0, r1) of A that `rank` uploads from host
     memory when every rank needs all of A, and the per-rank slot height

@@ -288,7 +288,7 @@ def launch_shape(gemm, M, N, K, info, library_arm):
         return dict(info, kernel="small_m_1cta", ctas=plan["tiles"] * split, threads_per_cta=192,
                     cluster=split)
     return dict(info, kernel="tiled", clusters=plan["clusters"], tiles=plan["tiles"],
-                threads_per_cta=576 if plan["tile_width"] == 512 else 192, cluster=2)
+                threads_per_cta=320 if plan["tile_width"] == 512 else 192, cluster=2)
 
 
 def roofline(w, M, N, K, ms_per_launch, peaks, peak_kind, traffic):
@@ -883,34 +883,51 @@ def run_strong16384(gemm, torch, dev, stream, args, barrier, distributed, world,
                             "how": "NCCL all_gather_into_tensor of the C shards (shard-major), timed "
                                    "separately from the GEMM, CUDA events, max over ranks"}
         del gathered
-        fused = shard.FusedAllGather(gemm, M, N)
-        try:
+        full = gemm.bf16_nt(A, B_full)  # the one-GPU 16384^3 result every rank's gathered C must equal
+        torch.cuda.synchronize()
+
+        def fused_leg(fused, how):
             fused.C.fill_(float("nan"))
             barrier()
             rc = fused.run(A, B, sptr)
             barrier()
-            full = gemm.bf16_nt(A, B_full)
-            torch.cuda.synchronize()
             same = torch.tensor([1 if rc == _lib.OK and torch.equal(
                 fused.view().view(torch.int16), full.view(torch.int16)) else 0], device=dev)
-            del full
             dist.all_reduce(same, op=dist.ReduceOp.MIN)
-            bit_exact = bool(same.item())
             fstep = lambda: fused.run(A, B, sptr)  # noqa: E731
             for _ in range(3):
                 fstep()
             barrier()
             fms = max_ms(time_steps(torch, fstep, reps, False, stream, dev, barrier)) / reps
-            res["fused_allgather"] = {
-                "ms": fms, "bit_exact": bit_exact, "tflops_aggregate": flops / (fms / 1e3) / 1e12,
-                "vs_gemm_plus_allgather": (ms / steps + ag_ms) / fms,
-                "how": "b200gemm_bf16_nt_allgather: the epilogue writes each C chunk into every rank's "
-                       "full-width C over NVLink (IPC-mapped peer stores); bit_exact: every rank's "
-                       "gathered C equals its own one-GPU 16384^3 GEMM, bit for bit"}
+            return {"ms": fms, "bit_exact": bool(same.item()), "tflops_aggregate": flops / (fms / 1e3) / 1e12,
+                    "vs_gemm_plus_allgather": (ms / steps + ag_ms) / fms, "how": how}
+
+        fused = shard.FusedAllGather(gemm, M, N)
+        try:
+            res["fused_allgather"] = fused_leg(
+                fused, "b200gemm_bf16_nt_allgather: the epilogue writes each C chunk into every rank's "
+                       "full-width C over NVLink (IPC-mapped peer stores); bit_exact: every rank's gathered "
+                       "C equals its own one-GPU 16384^3 GEMM, bit for bit")
         finally:
             barrier()
             fused.close()
             del fused
+        try:
+            mc = shard.MulticastAllGather(gemm, M, N)
+        except RuntimeError as e:
+            res["fused_allgather_multicast"] = {"unavailable": str(e)}
+            mc = None
+        if mc is not None:
+            try:
+                res["fused_allgather_multicast"] = fused_leg(
+                    mc, "b200gemm_bf16_nt_allgather_multicast: the epilogue writes each C chunk once with "
+                        "multimem.st to an NVLink multicast mapping of every rank's C (torch symmetric "
+                        "memory), NVSwitch replicates it; bit_exact as for fused_allgather")
+            finally:
+                barrier()
+                mc.close()
+                del mc
+        del full
     st, detail = gemm.last_device_status()
     if st != _lib.OK:
         raise RuntimeError(f"device status {st} {detail}")

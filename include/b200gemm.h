@@ -118,13 +118,27 @@ int b200gemm_bf16_nt_host(b200gemm_t handle, int M, int N, int K, const void* A,
  * writes every finished 32 x 32 chunk straight into the same place of each
  * peer's full-width C over NVLink (peer_C[i]: this rank's block inside peer
  * i's C, same ldc; device pointers from b200gemm_ipc_open), so the gather
- * overlaps the GEMM instead of following it.  npeers <= 7; N % 8 == 0.  When
+ * overlaps the GEMM instead of following it.  npeers <= 7; N % 8 == 0;
+ * K > 0 (with K == 0 the peers' blocks would not be written).  When
  * `stream` completes the local and peer writes are done; the peers still
  * need a barrier with this rank before reading.  Always uses the tiled
  * kernel.  No reference counterpart (the reference has no multi-GPU code). */
 int b200gemm_bf16_nt_allgather(b200gemm_t handle, int M, int N, int K, const void* A,
                                const void* B, void* C, int ldc, void* const* peer_C, int npeers,
                                void* stream);
+
+/* The same fused all-gather through an NVLink multicast (NVLS) mapping of
+ * every rank's full-width C: the epilogue writes each finished chunk once,
+ * with multimem.st, to mc_C (the multicast address of this rank's block,
+ * same ldc), and NVSwitch replicates it into every rank's C, this rank's
+ * own included (the local copy is not written separately; C is only
+ * described).  A multicast object spanning the ranks' C buffers comes from
+ * the caller, e.g. torch's symmetric memory (shard.MulticastAllGather).
+ * N % 8 == 0, K > 0, mc_C 16-byte aligned.  Every rank must keep its buffer
+ * bound until all ranks are done with it: tear down collectively.  No
+ * reference counterpart. */
+int b200gemm_bf16_nt_allgather_multicast(b200gemm_t handle, int M, int N, int K, const void* A,
+                                         const void* B, void* C, int ldc, void* mc_C, void* stream);
 
 /* CUDA IPC helpers for sharing device buffers between the processes of a
  * multi-GPU job: export a handle (B200GEMM_IPC_HANDLE_BYTES bytes) for the

@@ -85,3 +85,76 @@ def test_fused_allgather_matches_single_gpu(M, N, K, width):
         assert rc == 0, (rank, rc, same)
         assert same is True, (rank, same)
         assert status == 0, (rank, status)
+
+
+def _mc_worker(rank, world, port, M, N, K, q):
+    """The multicast form: every rank's C is one symmetric-memory buffer bound
+    to an NVLink multicast object; torn down collectively in every outcome."""
+    import datetime
+
+    import torch.distributed as dist
+
+    from b200_gemm_b200 import Gemm, data, shard
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                            timeout=datetime.timedelta(seconds=60))
+    gemm = Gemm(rank)
+    fused = None
+    try:
+        A, B = data.device_operands(M, N, K, "normal", seed=13, device=f"cuda:{rank}")
+        full = gemm.bf16_nt(A, B)
+        try:
+            fused = shard.MulticastAllGather(gemm, M, N)
+        except RuntimeError as e:
+            q.put((rank, "unsupported", str(e), 0))
+            return
+        B_local = B[fused.n0:fused.n1].contiguous()
+        fused.C.fill_(float("nan"))
+        torch.cuda.synchronize()
+        dist.barrier()
+        rcs = []
+        for _ in range(2):  # twice: the second call rewrites every block
+            rcs.append(fused.run(A, B_local, torch.cuda.current_stream().cuda_stream))
+        torch.cuda.synchronize()
+        dist.barrier()
+        same = bool(torch.equal(fused.view().contiguous().view(torch.int16), full.contiguous().view(torch.int16)))
+        status = gemm.last_device_status()[0]
+        q.put((rank, max(rcs), same, status))
+    except Exception as e:  # report instead of hanging the parent
+        q.put((rank, -1, repr(e), -1))
+    finally:
+        if fused is not None:
+            fused.close()
+        gemm.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("M,N,K", [(1024, 2048, 512), (600, 1536, 264)])
+def test_multicast_allgather_matches_single_gpu(M, N, K):
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("needs at least two GPUs")
+    world = min(n, 8)
+    ctx = torch.multiprocessing.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_mc_worker, args=(r, world, port, M, N, K, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    for _ in range(world):
+        r = q.get(timeout=300)
+        results[r[0]] = r[1:]
+    for p in procs:
+        p.join(timeout=120)
+        if p.is_alive():
+            p.kill()
+    if all(v[0] == "unsupported" for v in results.values()):
+        pytest.skip(f"no NVLink multicast on this node: {next(iter(results.values()))[1]}")
+    for rank, (rc, same, status) in results.items():
+        assert rc == 0, (rank, rc, same)
+        assert same is True, (rank, same)
+        assert status == 0, (rank, status)
