@@ -193,7 +193,7 @@ class Gemm:
                 "tail_split": out[4], "small_m_split": out[5]}
 
     def set_tail_half(self, enable: bool) -> None:
-        """Run a short last wave of 256 x 512 tiles as 256-column halves (default on)."""
+        """Run a short last wave of 256 x 512 (448) tiles as half-width tiles (default on)."""
         _lib.check(self._lib.b200gemm_set_tail_half(self._h, 1 if enable else 0), "b200gemm_set_tail_half")
 
     def set_tail_split(self, enable: bool) -> None:
@@ -202,8 +202,8 @@ class Gemm:
                    "b200gemm_set_tail_split")
 
     def set_tile_width(self, width: int) -> None:
-        """0 = choose per call (default), or 512, 256, 224, 192, 128 output
-        columns per 256-row tile."""
+        """0 = choose per call (default), or 512, 448, 256, 224, 192, 128
+        output columns per 256-row tile."""
         _lib.check(self._lib.b200gemm_set_tile_width(self._h, int(width)), "b200gemm_set_tile_width")
 
     def tile_width_for(self, M: int, N: int, K: int) -> int:

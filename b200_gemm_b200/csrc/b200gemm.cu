@@ -34,6 +34,10 @@ namespace b200gemm {
 #ifndef B200GEMM_L2_PROMOTION
 #define B200GEMM_L2_PROMOTION 3
 #endif
+// Time of a 256 x 448 tile relative to a 256 x 512 tile in the width model.
+#ifndef B200GEMM_TILE448_SCALE
+#define B200GEMM_TILE448_SCALE 0.9
+#endif
 #ifndef B200GEMM_DEFAULT_ORDER
 #define B200GEMM_DEFAULT_ORDER 1
 #endif
@@ -48,6 +52,11 @@ using CfgN256 = GemmCfg<B200GEMM_STAGES_N256, 1>;  // 256 x 256 tiles, overlappe
 using CfgN512 = GemmCfg<B200GEMM_STAGES_N512, 2, 256, false, B200GEMM_EPIWARPS_N512>;
 // The same tiles, launched only when a short last wave runs as 256-column halves.
 using CfgN512H = GemmCfg<B200GEMM_STAGES_N512, 2, 256, false, B200GEMM_EPIWARPS_N512, true>;
+// 256 x 448 tiles (two N = 224 MMAs per K step sharing the A stage), so a
+// shared-A tile also divides N = 1792 (the 8-way shard of N = 14336), and
+// their half-width form for a short last wave.
+using CfgN448 = GemmCfg<B200GEMM_STAGES_N512, 2, 224, false, B200GEMM_EPIWARPS_N512>;
+using CfgN448H = GemmCfg<B200GEMM_STAGES_N512, 2, 224, false, B200GEMM_EPIWARPS_N512, true>;
 // Narrower tiles for N that 256 does not divide into full waves (e.g. an
 // N-sharded projection with N = 1792 = 8 x 224); more stages fit because each
 // stage holds fewer B rows.
@@ -57,13 +66,14 @@ using CfgN128 = GemmCfg<8, 1, 128>;
 // The same five widths with the fused epilogue compiled in.
 using CfgE256 = GemmCfg<B200GEMM_STAGES_N256, 1, 256, true>;
 using CfgE512 = GemmCfg<4, 2, 256, true>;  // 8 epilogue warps: the fused math needs their registers
+using CfgE448 = GemmCfg<4, 2, 224, true>;
 using CfgE224 = GemmCfg<6, 1, 224, true>;
 using CfgE192 = GemmCfg<7, 1, 192, true>;
 using CfgE128 = GemmCfg<8, 1, 128, true>;
 // Tile widths of the tiled kernel, in the order the cost model prefers them
 // on a tie; index i of every per-width table below.
-constexpr int kWidths[] = {256, 512, 224, 192, 128};
-constexpr int kNumWidths = 5;
+constexpr int kWidths[] = {256, 512, 448, 224, 192, 128};
+constexpr int kNumWidths = 6;
 inline int width_index(int width) {
   for (int i = 0; i < kNumWidths; ++i)
     if (kWidths[i] == width) return i;
@@ -347,8 +357,10 @@ double tile_plan_cost(int width, uint32_t tiles_m, int N, int num_kb, int cluste
     const double feed = (16384.0 + 64.0 * w) / 32768.0;
     return num_kb * (0.08 + 0.92 * feed) / 0.85;
   };
-  if (width == 512) {
-    const double tile_time = (2.0 * num_kb + 17.0) * 0.8545 / 0.85;
+  if (width == 512 || width == 448) {
+    // 448: two N = 224 MMAs and 7/8 of the read-out per tile.
+    const double scale = width == 448 ? B200GEMM_TILE448_SCALE : 1.0;
+    const double tile_time = scale * (2.0 * num_kb + 17.0) * 0.8545 / 0.85;
     const uint64_t rem = tiles % static_cast<uint64_t>(clusters);
     if (half_tail && epi == 0.0 && rem > 0 && 2 * rem <= static_cast<uint64_t>(clusters)) {
       // The last wave runs as 256-column halves on their own 4-stage ring:
@@ -390,7 +402,8 @@ double epilogue_cost(const b200gemm_epilogue* epi, int width) {
     w512 += 2.0;
     w256 += 0.5;
   }
-  return width == 512 ? w512 : w256 * width / 256.0;
+  if (width == 512 || width == 448) return w512 * width / 512.0;
+  return w256 * width / 256.0;
 }
 
 }  // namespace b200gemm
@@ -487,14 +500,14 @@ extern "C" int b200gemm_create(b200gemm_t* out, int device) {
   if (tensor_map_encoder() == nullptr) return B200GEMM_ERR_CUDA;
   const int sms = prop.multiProcessorCount;
   const int cw[kNumWidths] = {prepare_kernel<CfgN256>(sms), prepare_kernel<CfgN512>(sms),
-                              prepare_kernel<CfgN224>(sms), prepare_kernel<CfgN192>(sms),
-                              prepare_kernel<CfgN128>(sms)};
+                              prepare_kernel<CfgN448>(sms), prepare_kernel<CfgN224>(sms),
+                              prepare_kernel<CfgN192>(sms), prepare_kernel<CfgN128>(sms)};
   const int ce[kNumWidths] = {prepare_kernel<CfgE256>(sms), prepare_kernel<CfgE512>(sms),
-                              prepare_kernel<CfgE224>(sms), prepare_kernel<CfgE192>(sms),
-                              prepare_kernel<CfgE128>(sms)};
+                              prepare_kernel<CfgE448>(sms), prepare_kernel<CfgE224>(sms),
+                              prepare_kernel<CfgE192>(sms), prepare_kernel<CfgE128>(sms)};
   for (int i = 0; i < kNumWidths; ++i)
     if (cw[i] <= 0 || ce[i] <= 0) return B200GEMM_ERR_CUDA;
-  if (prepare_kernel<CfgN512H>(sms) <= 0) return B200GEMM_ERR_CUDA;
+  if (prepare_kernel<CfgN512H>(sms) <= 0 || prepare_kernel<CfgN448H>(sms) <= 0) return B200GEMM_ERR_CUDA;
   const int dc1 = prepare_decode_kernel<DecodeCfg<1>>(sms), dc2 = prepare_decode_kernel<DecodeCfg<2>>(sms),
             dc4 = prepare_decode_kernel<DecodeCfg<4>>(sms);
   if (dc1 <= 0 || dc2 <= 0 || dc4 <= 0) return B200GEMM_ERR_CUDA;
@@ -691,7 +704,7 @@ int tail_half_for(const b200gemm_handle* h, int tiles, int clusters) {
 // Instances that carry the K-split tail (GemmCfg::kTailSplit): the plain
 // ones except the 512-wide, whose 16 epilogue warps leave it no registers.
 bool tail_split_width(int width, bool fused) {
-  return !fused && (width == 512 ? CfgN512::kTailSplit : true);
+  return !fused && (width == 512 ? CfgN512::kTailSplit : (width == 448 ? CfgN448::kTailSplit : true));
 }
 
 // Tile width (one of kWidths) a call on this handle will use: the cheapest
@@ -713,17 +726,25 @@ int choose_tile_width(const b200gemm_handle* h, int M, int N, int K,
       best = kWidths[i];
     }
   }
-  // 256 x 512 tiles with a half-width last wave replace the choice only when
+  // Shared-A tiles with a half-width last wave replace the choice only when
   // clearly cheaper (3%): the model's margin of error is about that.
-  if (best != 512 && h->tail_half_enabled && epi == nullptr) {
-    const double c = tile_plan_cost(512, tiles_m, N, num_kb, clusters[width_index(512)], 0.0, true);
-    if (c < 0.97 * best_cost) best = 512;
+  if (h->tail_half_enabled && epi == nullptr) {
+    const int base = best;
+    double best_half = 0.97 * best_cost;
+    for (int w : {512, 448}) {
+      if (w == base) continue;
+      const double c = tile_plan_cost(w, tiles_m, N, num_kb, clusters[width_index(w)], 0.0, true);
+      if (c < best_half) {
+        best_half = c;
+        best = w;
+      }
+    }
   }
   return best;
 }
 
 // B rows of one CTA's tensor-map box for a tile width.
-int b_box_rows(int width) { return width == 512 ? 128 : width / 2; }
+int b_box_rows(int width) { return width > 256 ? width / 4 : width / 2; }
 
 cudaError_t launch_width(int width, bool fused, int clusters, cudaStream_t stream,
                          const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc,
@@ -731,6 +752,7 @@ cudaError_t launch_width(int width, bool fused, int clusters, cudaStream_t strea
   if (fused) {
     switch (width) {
       case 512: return launch_gemm<CfgE512>(clusters, stream, ma, mb, mc, p);
+      case 448: return launch_gemm<CfgE448>(clusters, stream, ma, mb, mc, p);
       case 224: return launch_gemm<CfgE224>(clusters, stream, ma, mb, mc, p);
       case 192: return launch_gemm<CfgE192>(clusters, stream, ma, mb, mc, p);
       case 128: return launch_gemm<CfgE128>(clusters, stream, ma, mb, mc, p);
@@ -741,6 +763,9 @@ cudaError_t launch_width(int width, bool fused, int clusters, cudaStream_t strea
     case 512:
       return p.tail_half ? launch_gemm<CfgN512H>(clusters, stream, ma, mb, mc, p)
                          : launch_gemm<CfgN512>(clusters, stream, ma, mb, mc, p);
+    case 448:
+      return p.tail_half ? launch_gemm<CfgN448H>(clusters, stream, ma, mb, mc, p)
+                         : launch_gemm<CfgN448>(clusters, stream, ma, mb, mc, p);
     case 224: return launch_gemm<CfgN224>(clusters, stream, ma, mb, mc, p);
     case 192: return launch_gemm<CfgN192>(clusters, stream, ma, mb, mc, p);
     case 128: return launch_gemm<CfgN128>(clusters, stream, ma, mb, mc, p);
@@ -1184,7 +1209,7 @@ int gemm_device(b200gemm_t h, int M, int N, int K, const void* A, const void* B,
 
   // 256 x 512 tiles: a last wave of at most half as many tiles as clusters
   // runs as 256-column halves on twice the clusters (plain epilogue only).
-  if (!tail_on && width == 512 && !fused && tail_half_for(h, p.num_tiles, max_clusters) > 0) {
+  if (!tail_on && (width == 512 || width == 448) && !fused && tail_half_for(h, p.num_tiles, max_clusters) > 0) {
     const int rem = tail_half_for(h, p.num_tiles, max_clusters);
     p.tail_start = p.num_tiles - rem;
     p.tail_half = 1;
@@ -1221,7 +1246,7 @@ extern "C" int b200gemm_plan(b200gemm_t h, int M, int N, int K, int* plan) {
   const int maxc = h->clusters_w[width_index(width)];
   const int num_kb = (K + kBlockK - 1) / kBlockK;
   const int sk = (h->tail_split_enabled && tail_split_width(width, false)) ? tail_split_for(tiles, maxc, num_kb) : 1;
-  const int halves = (sk < 2 && width == 512) ? tail_half_for(h, tiles, maxc) : 0;
+  const int halves = (sk < 2 && (width == 512 || width == 448)) ? tail_half_for(h, tiles, maxc) : 0;
   const int units = tiles + (sk >= 2 ? (tiles % maxc) * (sk - 1) : 0) + halves;
   const int clusters = units < maxc ? units : maxc;
   plan[0] = 1;  // tiled kernel

@@ -102,7 +102,7 @@ struct GemmParams {
   int tail_start;
   int tail_split;       // 1 = no split
   int tail_kb;
-  // 256 x 512 tiles only: with tail_half, unit tail_start + 2 r + h is the
+  // Shared-A tiles (NB = 2) only: with tail_half, unit tail_start + 2 r + h is the
   // h-th 256-column half of tile tiles[tail_start + r] over the whole of K,
   // so a last wave of up to half the clusters' tiles runs in about half a
   // tile's time on twice the clusters.
@@ -173,9 +173,11 @@ __device__ __forceinline__ WorkUnit unit_at(const GemmParams& p, uint32_t u) {
 // Compile-time shape of one kernel instance.
 //   NB = 1: a pair computes 256 x 256 tiles; TMEM holds two accumulators, so
 //           the MMA of tile i+1 overlaps the epilogue of tile i.
-//   NB = 2: a pair computes 256 x 512 tiles as two N = 256 MMAs per K step
-//           that share the A stage: 25% fewer operand bytes into each SM per
-//           flop; the single 512-column accumulator is drained by EW warps.
+//   NB = 2: a pair computes 256 x 2MN tiles (MN = 256 or 224) as two N = MN
+//           MMAs per K step that share the A stage: 25% fewer operand bytes
+//           into each SM per flop than 256 x 256 tiles; the single 2MN-column
+//           accumulator is drained by EW warps.  256 x 448 tiles divide
+//           N = 1792 (the 8-way shard of a 14336-wide MLP projection).
 //   MN (NB = 1 only): columns of one MMA and of the tile, a multiple of 32
 //           up to 256 (e.g. 224 = 1792 / 8 for an N-sharded MLP projection),
 //           so the tile width can divide N and fill the last wave.
@@ -189,7 +191,7 @@ __device__ __forceinline__ WorkUnit unit_at(const GemmParams& p, uint32_t u) {
 template <int STAGES, int NB, int MN = 256, bool EPI = false, int EW = 4 * NB, bool HALF = false>
 struct GemmCfg {
   static_assert(NB == 1 || NB == 2, "one or two MMA column blocks per tile");
-  static_assert(MN % 32 == 0 && MN >= 64 && MN <= 256 && (NB == 1 || MN == 256), "MMA width");
+  static_assert(MN % 32 == 0 && MN >= 64 && MN <= 256 && (NB == 1 || MN == 256 || MN == 224), "MMA width");
   static constexpr int kStages = STAGES;
   static constexpr int kNB = NB;
   static constexpr bool kEpi = EPI;
@@ -227,8 +229,7 @@ struct GemmCfg {
   // after the TMEM reads alone (epilogue of gemm_bf16_nt_sm100).  Loads go
   // in pairs.
   static constexpr int kHeldChunks = kWarpChunks - kCBufs;
-  static constexpr bool kStagedDrain =
-      !EPI && NB == 2 && kCBufs % 2 == 0 && kHeldChunks > 0 && kHeldChunks % 2 == 0;
+  static constexpr bool kStagedDrain = !EPI && NB == 2 && kHeldChunks > 0;
   static constexpr int kStageBytesB = kBlockBytesB * NB;
   static constexpr uint32_t kTxBytes = 2 * (kStageBytesA + kStageBytesB);  // both CTAs
   // shared memory layout (offsets from a 1024-byte aligned base)
@@ -1006,26 +1007,29 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1) __cluster_dims__(2, 1, 1)
             for (int c = 0; c < kStaged; c += 2) {
               uint32_t v0[32], v1[32];
               ptx::tmem_ld_32x32b_x32(t_row + c * kCBoxCols, v0);
-              ptx::tmem_ld_32x32b_x32(t_row + (c + 1) * kCBoxCols, v1);
+              if (c + 1 < kStaged) ptx::tmem_ld_32x32b_x32(t_row + (c + 1) * kCBoxCols, v1);
               ptx::tmem_wait_ld();
               ptx::reg_fence32(v0);
-              ptx::reg_fence32(v1);
               stage_chunk_row_f32(cstage0 + c * kCStageBytes, lane, v0);
-              stage_chunk_row_f32(cstage0 + (c + 1) * kCStageBytes, lane, v1);
+              if (c + 1 < kStaged) {
+                ptx::reg_fence32(v1);
+                stage_chunk_row_f32(cstage0 + (c + 1) * kCStageBytes, lane, v1);
+              }
             }
             uint32_t pk[kHeld][16];
 #pragma unroll
             for (int h = 0; h < kHeld; h += 2) {
               uint32_t v0[32], v1[32];
               ptx::tmem_ld_32x32b_x32(t_row + (kStaged + h) * kCBoxCols, v0);
-              ptx::tmem_ld_32x32b_x32(t_row + (kStaged + h + 1) * kCBoxCols, v1);
+              if (h + 1 < kHeld) ptx::tmem_ld_32x32b_x32(t_row + (kStaged + h + 1) * kCBoxCols, v1);
               ptx::tmem_wait_ld();
               ptx::reg_fence32(v0);
-              ptx::reg_fence32(v1);
 #pragma unroll
-              for (int i = 0; i < 16; ++i) {
-                pk[h][i] = ptx::pack_bf16x2(v0[2 * i], v0[2 * i + 1]);
-                pk[h + 1][i] = ptx::pack_bf16x2(v1[2 * i], v1[2 * i + 1]);
+              for (int i = 0; i < 16; ++i) pk[h][i] = ptx::pack_bf16x2(v0[2 * i], v0[2 * i + 1]);
+              if (h + 1 < kHeld) {
+                ptx::reg_fence32(v1);
+#pragma unroll
+                for (int i = 0; i < 16; ++i) pk[h + 1][i] = ptx::pack_bf16x2(v1[2 * i], v1[2 * i + 1]);
               }
             }
             // Every TMEM read of this warp is done: release the accumulator.

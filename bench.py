@@ -21,7 +21,9 @@ Every run also carries a "strong16384" block (skip with --no-strong): the
 whole 16384^3), its separately timed NCCL all-gather of C and the GEMM with
 the all-gather fused into its epilogue (checked bit for bit against a
 single-GPU GEMM first), and its end-to-end rate from host memory, where each
-rank uploads only its share of A's rows and gathers the rest over NVLink.
+rank uploads only its share of A's rows and gathers the rest over NVLink;
+and a "strong_mlp" block: the MLP projection 16384 x 14336 x 4096 split the
+same way (configs[3] of the benchmark at 8 GPUs).
 
 --impl reference times the reference implementation of the path on the
 host CPU cores: the reference project has no CPU GEMM of its own, so this
@@ -76,7 +78,7 @@ def parse_args(argv=None):
     p.add_argument("--impl", default="ours", choices=["ours", "reference", "cublaslt"],
                    help="ours: this library; reference: the reference arithmetic on the host CPU; "
                         "cublaslt: torch.matmul with the cuBLASLt backend on the same operands")
-    p.add_argument("--tile-width", type=int, default=0, choices=[0, 512, 256, 224, 192, 128],
+    p.add_argument("--tile-width", type=int, default=0, choices=[0, 512, 448, 256, 224, 192, 128],
                    help="force the output tile width (0 = the library's per-shape choice)")
     p.add_argument("--order", default="default", choices=["default", "hilbert", "bands"])
     p.add_argument("--band", type=int, default=16, help="tile-rows per band for --order bands")
@@ -91,7 +93,7 @@ def parse_args(argv=None):
     p.add_argument("--no-cublas", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
-    p.add_argument("--no-strong", action="store_true", help="skip the strong16384 block")
+    p.add_argument("--no-strong", action="store_true", help="skip the strong16384 and strong_mlp blocks")
     p.add_argument("--no-numa-bind", action="store_true",
                    help="do not move each rank onto the CPUs of its GPU's NUMA node")
     p.add_argument("--cpu-seconds", type=float, default=10.0,
@@ -288,7 +290,7 @@ def launch_shape(gemm, M, N, K, info, library_arm):
         return dict(info, kernel="small_m_1cta", ctas=plan["tiles"] * split, threads_per_cta=192,
                     cluster=split)
     return dict(info, kernel="tiled", clusters=plan["clusters"], tiles=plan["tiles"],
-                threads_per_cta=320 if plan["tile_width"] == 512 else 192, cluster=2)
+                threads_per_cta=320 if plan["tile_width"] > 256 else 192, cluster=2)
 
 
 def roofline(w, M, N, K, ms_per_launch, peaks, peak_kind, traffic):
@@ -682,6 +684,8 @@ def run_ours(args, w):
         torch.cuda.empty_cache()
         extra["strong16384"] = run_strong16384(gemm, torch, dev, stream, args, barrier, distributed,
                                                world, rank)
+        torch.cuda.empty_cache()
+        extra["strong_mlp"] = run_strong_mlp(gemm, torch, dev, stream, args, barrier, distributed, world, rank)
     info = gemm.device_info()
     result = None
     if rank == 0:
@@ -816,23 +820,19 @@ def run_e2e(gemm, torch, dev, stream, M, Nl, K, A, B, args, barrier, distributed
                          "waits for the second before the end event; max over ranks"}
 
 
-def run_strong16384(gemm, torch, dev, stream, args, barrier, distributed, world, rank):
-    """The north-star scaling configuration: C = A . B^T at M = N = K = 16384
-    (N(0,1) operands), B and C column-sharded over all ranks, A replicated
-    (at one GPU the whole GEMM).  Times the GEMM (max over ranks, aggregate
-    TFLOPS), the NCCL all-gather of the C shards separately, the GEMM with
-    the all-gather fused into its epilogue (b200gemm_bf16_nt_allgather; first
-    checked bit for bit on every rank against a one-GPU 16384^3 GEMM), and
-    the end-to-end rate from pinned host memory (host_e2e)."""
+def strong_gemm(gemm, torch, dev, stream, args, barrier, distributed, world, rank, M, N, K, dist_name,
+                seed):
+    """C = A . B^T split along N over all ranks (strong scaling; at one GPU
+    the whole GEMM): B and C column-sharded, A replicated, no collective.
+    Returns (result dict, A, B_local, B_full, C_local, ms for the steps, steps)."""
     import torch.distributed as dist
 
     from b200_gemm_b200 import _lib, data, shard
 
-    M = N = K = 16384
     n0, n1 = shard.column_shard(N, world, rank)
     Nl = n1 - n0
     flops = 2.0 * M * N * K
-    A, B_full = data.device_operands(M, N, K, "normal", seed=args.seed + 100, device=dev)
+    A, B_full = data.device_operands(M, N, K, dist_name, seed=seed, device=dev)
     B = B_full[n0:n1].contiguous() if Nl != N else B_full
     C = torch.empty(M, Nl, dtype=torch.bfloat16, device=dev)
     sptr = int(stream.cuda_stream)
@@ -843,25 +843,63 @@ def run_strong16384(gemm, torch, dev, stream, args, barrier, distributed, world,
         if rc != _lib.OK:
             raise RuntimeError(_lib.strerror(rc))
 
-    def max_ms(ms):
-        if not distributed:
-            return ms
-        t = torch.tensor([ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
     steps = max(5, min(args.steps, 20))
     for _ in range(3):
         step()
     barrier()
-    ms = max_ms(time_steps(torch, step, steps, False, stream, dev, barrier))
+    ms = time_steps(torch, step, steps, False, stream, dev, barrier)
+    if distributed:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    st, detail = gemm.last_device_status()
+    if st != _lib.OK:
+        raise RuntimeError(f"device status {st} {detail}")
     plan = gemm.plan(M, Nl, K)
-    res = {"M": M, "N": N, "K": K, "N_per_gpu": Nl, "n_gpus": world, "dist": "normal",
+    res = {"M": M, "N": N, "K": K, "N_per_gpu": Nl, "n_gpus": world, "dist": dist_name,
            "scaling": "strong", "steps": steps, "ms_per_step": ms / steps,
            "value": flops / (ms / 1e3 / steps) / 1e12, "unit": "TFLOPS",
            "tile_width": plan["tile_width"], "tail_split": plan["tail_split"],
            "how": "B and C column-sharded (shard.column_shard), A replicated, no collective; back-to-back "
-                  "launches, CUDA events, max over ranks; value = 2*16384^3 / per-step time"}
+                  "launches, CUDA events, max over ranks; value = 2MNK / per-step time"}
+    return res, A, B, B_full, C, ms, steps
+
+
+def run_strong_mlp(gemm, torch, dev, stream, args, barrier, distributed, world, rank):
+    """the MLP projection 16384 x 14336 x 4096 (A ~ N(0,1)
+    activations, B ~ N(0,0.02) weights) split along N over all ranks."""
+    res, A, B, B_full, C, _, _ = strong_gemm(gemm, torch, dev, stream, args, barrier, distributed, world,
+                                             rank, 16384, 14336, 4096, "mlp", args.seed + 200)
+    del A, B, B_full, C
+    return res
+
+
+def run_strong16384(gemm, torch, dev, stream, args, barrier, distributed, world, rank):
+    """The north-star scaling configuration: C = A . B^T at M = N = K = 16384
+    (N(0,1) operands), B and C column-sharded over all ranks, A replicated
+    (at one GPU the whole GEMM).  Times the GEMM (max over ranks, aggregate
+    TFLOPS), the NCCL all-gather of the C shards separately, the GEMM with
+    the all-gather fused into its epilogue (P2P stores and NVLink multicast;
+    each first checked bit for bit on every rank against a one-GPU 16384^3
+    GEMM), and the end-to-end rate from pinned host memory (host_e2e)."""
+    import torch.distributed as dist
+
+    from b200_gemm_b200 import _lib, shard
+
+    M = N = K = 16384
+    flops = 2.0 * M * N * K
+    res, A, B, B_full, C, ms, steps = strong_gemm(gemm, torch, dev, stream, args, barrier, distributed,
+                                                  world, rank, M, N, K, "normal", args.seed + 100)
+    Nl = res["N_per_gpu"]
+    sptr = int(stream.cuda_stream)
+
+    def max_ms(v):
+        if not distributed:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
     reps = max(3, min(args.steps, 20))
     if distributed:
         gathered = torch.empty(world * M * Nl, dtype=torch.bfloat16, device=dev)

@@ -182,9 +182,10 @@ int b200gemm_device_info(b200gemm_t handle, int* sm_count, int* max_clusters);
 /* Output tile width of the handle's GEMM calls: 256 (256 x 256 tiles, two
  * TMEM accumulators so a tile's epilogue overlaps the next tile's MMAs), 512
  * (256 x 512 tiles: one A stage feeds two MMAs, a quarter less operand
- * traffic per flop), 224, 192 or 128 (narrower 256-row tiles, for N that
- * wider tiles split into a partly idle last wave, e.g. N = 1792 = 8 x 224),
- * or 0 (default) to choose per call from the shape.  Any other value is
+ * traffic per flop), 448 (the same with two N = 224 MMAs, so a shared-A tile
+ * divides N = 1792 = 4 x 448), 224, 192 or 128 (narrower 256-row tiles, for
+ * N that wider tiles split into a partly idle last wave), or 0 (default) to
+ * choose per call from the shape.  Any other value is
  * B200GEMM_ERR_INVALID_ARG.  The reference has one fixed 256 x 256
  * configuration (matmul_1.cuh:13-22). */
 int b200gemm_set_tile_width(b200gemm_t handle, int width);
@@ -198,7 +199,8 @@ int b200gemm_set_tile_width(b200gemm_t handle, int width);
  * an event (they share the workspace).  No reference counterpart. */
 int b200gemm_set_tail_split(b200gemm_t handle, int enable);
 
-/* Run a short last wave of 256 x 512 tiles as 256-column halves (default
+/* Run a short last wave of 256 x 512 (256 x 448) tiles as 256-column
+ * (224-column) halves (default
  * on): when T tiles leave R = T mod G of G clusters busy in the last wave and
  * 2R <= G, each of those R tiles runs as two half tiles over the whole of K on
  * 2R clusters, so that wave takes about half a tile's time.  Plain epilogue
@@ -210,10 +212,10 @@ int b200gemm_set_tail_half(b200gemm_t handle, int enable);
  * rows of B per CTA), tile width (tiled) or rows of B per cluster (small-M),
  * tiles, clusters launched, how the tiles of the last partial wave are cut
  * (tiled kernel: 1 = not at all, S >= 2 = into S K slices, -2 = into two
- * 256-column halves), K split of the small-M kernel. */
+ * half-width tiles), K split of the small-M kernel. */
 int b200gemm_plan(b200gemm_t handle, int M, int N, int K, int* plan);
 
-/* The tile width (512, 256, 224, 192 or 128) a call with this shape would
+/* The tile width (512, 448, 256, 224, 192 or 128) a call with this shape would
  * use now; 0 for an invalid handle or shape. */
 int b200gemm_tile_width_for(b200gemm_t handle, int M, int N, int K);
 

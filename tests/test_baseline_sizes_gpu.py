@@ -4,7 +4,7 @@ C-ABI, for the kernel instance each shape actually gets:
   * MLP projection 16384 x 14336 x 4096 (A ~ N(0,1) activations, B ~
     N(0,0.02) weights): the width the cost model picks (256 x 512 tiles) and
     forced 256-wide tiles;
-  * its 8-way N shard 16384 x 1792 x 4096 (224-wide tiles);
+  * its 8-way N shard 16384 x 1792 x 4096 (448- and 224-wide tiles);
   * 16384^3 on one GPU (256 x 512 tiles, 28 waves);
   * its 8-way N shard 16384 x 2048 x 16384 (256 x 512 tiles whose short last
     wave runs as 256-column halves on the re-cut 4-stage ring, K = 16384).
@@ -86,12 +86,19 @@ def test_mlp_16384x14336x4096_auto_and_256(gpu_handle, oracle_mod):
     _check_vs_oracle(C256, A, B, oracle_mod, seed=2)
 
 
-def test_mlp_shard_16384x1792x4096_width_224(gpu_handle, oracle_mod):
+def test_mlp_shard_16384x1792x4096_widths_448_and_224(gpu_handle, oracle_mod):
+    """The 8-way shard of the MLP projection: the chosen width (a tile width
+    that divides 1792: 448 with a half-width last wave, or 224), and both
+    forced, bit-identical to each other."""
     M, N, K = 16384, 1792, 4096
     A, B, C, plan = _run(gpu_handle, M, N, K, "mlp", seed=32)
-    assert plan["tile_width"] == 224, plan
+    assert plan["tile_width"] in (448, 224), plan
     _check_vs_cublaslt(C, A, B)
     _check_vs_oracle(C, A, B, oracle_mod, seed=3)
+    for width in (448, 224):
+        _, _, Cw, planw = _run(gpu_handle, M, N, K, "mlp", seed=32, width=width)
+        assert planw["tile_width"] == width, planw
+        assert torch.equal(C.view(torch.int16), Cw.view(torch.int16)), f"width {width} differs"
 
 
 def test_square_16384_one_gpu(gpu_handle, oracle_mod):

@@ -65,7 +65,7 @@ SHAPES = [
 ]
 
 
-WIDTHS = [256, 512, 224, 192, 128]
+WIDTHS = [256, 512, 448, 224, 192, 128]
 
 
 @pytest.fixture(params=WIDTHS, ids=[f"w{w}" for w in WIDTHS])
@@ -135,8 +135,10 @@ def test_tile_width_selection(gpu_handle):
     h = gpu_handle
     assert h.tile_width_for(8192, 8192, 8192) == 512
     assert h.tile_width_for(256, 256, 64) in WIDTHS
-    # N-sharded MLP projection: 1792 = 8 x 224 columns fill the last wave
-    assert h.tile_width_for(16384, 1792, 4096) == 224
+    # N-sharded MLP projection: 1792 = 4 x 448 columns of shared-A tiles,
+    # their 34-tile last wave cut into 224-column halves
+    assert h.tile_width_for(16384, 1792, 4096) == 448
+    assert h.plan(16384, 1792, 4096)["tail_split"] == -2
     # 16384^3 sharded over 8 GPUs: 256 x 512 tiles with their 34-tile last
     # wave cut into 256-column halves; short K keeps 256-wide tiles
     assert h.tile_width_for(16384, 2048, 16384) == 512

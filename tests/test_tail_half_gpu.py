@@ -17,21 +17,25 @@ def _bits(t):
     return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
 
 
-# (M, N, K): 256 tiles (a last wave of 34 on 74 clusters); 16 tiles (one
-# partial wave, all halves); ragged 36 tiles whose last column is cut at N.
-CASES = [(16384, 2048, 1024), (512, 4096, 512), (3000, 1496, 264)]
+# (width, M, N, K).  256 x 512: 256 tiles (a last wave of 34 on 74
+# clusters); 16 tiles (one partial wave, all halves); ragged 36 tiles whose
+# last column is cut at N.  256 x 448 (halves of 224 columns): 256 tiles of
+# the 8-way MLP shard width N = 1792; 20 tiles (all halves); ragged M and N,
+# 36 tiles.
+CASES = [(512, 16384, 2048, 1024), (512, 512, 4096, 512), (512, 3000, 1496, 264),
+         (448, 16384, 1792, 1024), (448, 512, 4480, 512), (448, 3000, 1304, 264)]
 
 
-@pytest.mark.parametrize("M,N,K", CASES)
-def test_half_tail_bit_exact_and_oracle(gpu_handle, oracle_mod, M, N, K):
+@pytest.mark.parametrize("width,M,N,K", CASES)
+def test_half_tail_bit_exact_and_oracle(gpu_handle, oracle_mod, width, M, N, K):
     h = gpu_handle
-    h.set_tile_width(512)
+    h.set_tile_width(width)
     try:
         h.set_tail_half(False)
         plan0 = h.plan(M, N, K)
         h.set_tail_half(True)
         plan1 = h.plan(M, N, K)
-        assert plan1["tile_width"] == 512 and plan1["tiles"] == plan0["tiles"]
+        assert plan1["tile_width"] == width and plan1["tiles"] == plan0["tiles"]
         assert (plan0["tail_split"], plan1["tail_split"]) == (1, -2), (plan0, plan1)
         assert plan1["clusters"] >= plan0["clusters"], (plan0, plan1)
         A, B = data.device_operands(M, N, K, "normal", seed=M + N + K)
