@@ -512,8 +512,8 @@ extern "C" int b200gemm_create(b200gemm_t* out, int device) {
             dc4 = prepare_decode_kernel<DecodeCfg<4>>(sms);
   if (dc1 <= 0 || dc2 <= 0 || dc4 <= 0) return B200GEMM_ERR_CUDA;
   const int dw1 = prepare_decode_kernel<DecodeCfg<1, 256>>(sms), dw2 = prepare_decode_kernel<DecodeCfg<2, 256>>(sms),
-            dw4 = prepare_decode_kernel<DecodeCfg<4, 256>>(sms);
-  if (dw1 <= 0 || dw2 <= 0 || dw4 <= 0) return B200GEMM_ERR_CUDA;
+            dw3 = prepare_decode_kernel<DecodeCfg<3, 256>>(sms), dw4 = prepare_decode_kernel<DecodeCfg<4, 256>>(sms);
+  if (dw1 <= 0 || dw2 <= 0 || dw3 <= 0 || dw4 <= 0) return B200GEMM_ERR_CUDA;
   const int sc2 = prepare_smallm1_kernel<SmallMCfg<2>>(sms), sc4 = prepare_smallm1_kernel<SmallMCfg<4>>(sms);
   if (sc2 <= 0 || sc4 <= 0) return B200GEMM_ERR_CUDA;
 
@@ -525,6 +525,7 @@ extern "C" int b200gemm_create(b200gemm_t* out, int device) {
   h->decode_clusters[4] = dc4;
   h->decode256_clusters[1] = dw1;
   h->decode256_clusters[2] = dw2;
+  h->decode256_clusters[3] = dw3;
   h->decode256_clusters[4] = dw4;
   h->smallm1_clusters[2] = sc2;
   h->smallm1_clusters[4] = sc4;
@@ -779,20 +780,29 @@ namespace {
 
 // K split for the small-M kernel, or 0 when the tiled kernel should run:
 // M <= 256, N % 8 == 0 (its C stores are whole 16-byte groups), and the
-// largest S in {4, 2} whose N / 256 clusters of 2S CTAs are all co-resident
-// (decode_clusters[S] for M <= 128, decode256_clusters[S] above, from the
-// occupancy query: a cluster must fit in one GPC, so fewer than sm_count / 2S
-// fit, and a second wave would double the time) while every CTA pair keeps
-// at least two K blocks, else 1.
+// largest S in {4, 3, 2} ({4, 2} for M <= 128, whose 128 rows of A do not
+// cut into three 32-row-aligned slices) whose N / 256 clusters of 2S CTAs are
+// all co-resident (decode_clusters[S] for M <= 128, decode256_clusters[S]
+// above, from the occupancy query: a cluster must fit in one GPC, so fewer
+// than sm_count / 2S fit, and a second wave would double the time) while
+// every CTA pair keeps at least two K blocks, else 1.  A split of 3 covers
+// N = 4096 at 129..256 rows, where 16 clusters of 8 CTAs do not fit.
 int decode_split(const b200gemm_handle* h, int M, int N, int K) {
   if (M > 256 || (N % 8) != 0 || K < 2 * kBlockK) return 0;
   const int clusters = (N + 255) / 256;
   const int num_kb = (K + kBlockK - 1) / kBlockK;
   const int* fit = M > 128 ? h->decode256_clusters : h->decode_clusters;
-  for (int s : {4, 2}) {
+  for (int s : {4, 3, 2}) {
+    if (s == 3 && M <= 128) continue;
     if (clusters <= fit[s] && num_kb >= 2 * s) return s;
   }
   return 1;
+}
+
+// Rows of C per CTA pair of the pair kernel (the map box height of C and of
+// the residual): DecodeCfg<S, NT>::kSliceRows.
+uint32_t decode_slice_rows(int nt, int split) {
+  return static_cast<uint32_t>((nt / split + 31) / 32 * 32);
 }
 
 // Which small-M kernel a shape takes: kind 0 = none (tiled kernel), 2 = the
@@ -907,7 +917,7 @@ int run_decode(b200gemm_t h, int split, int M, int N, int K, const void* A, cons
   const uint64_t k = static_cast<uint64_t>(K);
   CUtensorMap ma, mb, mc, mr;
   const int nt = M > 128 ? 256 : 128;  // rows of A one MMA covers
-  const uint32_t slice_rows = static_cast<uint32_t>(nt / split);
+  const uint32_t slice_rows = decode_slice_rows(nt, split);
   const EpiArgs ea = epi_args(epi);
   if (!encode_2d(&ma, A, k, static_cast<uint64_t>(M), k * 2, kBlockK, nt / 2, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !encode_2d(&mb, B, k, static_cast<uint64_t>(N), k * 2, kBlockK, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
@@ -930,6 +940,7 @@ int run_decode(b200gemm_t h, int split, int M, int N, int K, const void* A, cons
   cudaError_t e;
   if (nt == 256) {
     if (split == 4) e = launch_decode<DecodeCfg<4, 256>>(stream, ma, mb, mc, mr, p);
+    else if (split == 3) e = launch_decode<DecodeCfg<3, 256>>(stream, ma, mb, mc, mr, p);
     else if (split == 2) e = launch_decode<DecodeCfg<2, 256>>(stream, ma, mb, mc, mr, p);
     else e = launch_decode<DecodeCfg<1, 256>>(stream, ma, mb, mc, mr, p);
   } else {

@@ -45,8 +45,9 @@ struct DecodeParams {
 // NT = rows of A covered (the MMA's N): 128 for M <= 128, 256 for M <= 256.
 template <int S, int NT = 128>
 struct DecodeCfg {
-  static_assert(S == 1 || S == 2 || S == 4, "split factor");
+  static_assert(S == 1 || S == 2 || S == 3 || S == 4, "split factor");
   static_assert(NT == 128 || NT == 256, "rows of A per MMA");
+  static_assert(S != 3 || NT == 256, "a split of 3 slices 256 rows of A as 96 + 96 + 64");
   static constexpr int kSplit = S;
   static constexpr int kNT = NT;
   static constexpr int kClusterSize = 2 * S;
@@ -62,7 +63,14 @@ struct DecodeCfg {
   static constexpr int kStageB = kKps * kSubB;
   static constexpr int kStageA = kKps * kSubA;
   static constexpr int kStageBytes = kStageB + kStageA;
-  static constexpr int kSliceRows = kNT / S;                 // rows of C each CTA finishes
+  // Rows of C (rows of A) each CTA pair finishes: kSliceRows for every pair
+  // but the last, which takes the rest (S = 3: 96, 96, 64).  Slices are
+  // whole 32-row chunks, and only the last may be shorter, so a C or residual
+  // box of kSliceRows rows from the last slice's first row overhangs only
+  // rows >= 256 >= M, which TMA clips (stores) or zero-fills (loads).
+  static constexpr int kSliceRows = (kNT / S + 31) / 32 * 32;
+  static constexpr int kLastSliceRows = kNT - (S - 1) * kSliceRows;
+  static_assert(kLastSliceRows > 0 && kLastSliceRows <= kSliceRows && kLastSliceRows % 32 == 0, "slices");
   static constexpr int kRecvSlotBytes = 128 * kSliceRows * 4;  // [kSliceRows/4][128 rows][4] fp32
   static constexpr int kRecvBytes = (S - 1) * kRecvSlotBytes;
   static constexpr int kCWarpBytes = kSliceRows * 32 * 4;    // kSliceRows x 32 outputs (up to fp32) per warp
@@ -111,6 +119,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   const uint32_t rank = ptx::cluster_ctarank();
   const uint32_t pair = rank >> 1, half = rank & 1u;
+  auto slice_rows = [](uint32_t pr) {
+    return pr + 1 == static_cast<uint32_t>(S) ? Cfg::kLastSliceRows : Cfg::kSliceRows;
+  };
   const bool leader = half == 0;
   const int n0 = static_cast<int>(ptx::cluster_id_x()) * 256;
   const int kb_begin = static_cast<int>(pair) * p.kb_per_split;
@@ -142,7 +153,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     ptx::fence_mbar_init_cluster();
     // The partner pairs' partial slices arrive as counted bytes; the one
     // arrival is this expect_tx, made before any partner can send.
-    if (S > 1) ptx::mbar_arrive_expect_tx(recv_bar, Cfg::kRecvBytes);
+    if (S > 1) ptx::mbar_arrive_expect_tx(recv_bar, (S - 1) * 128 * 4 * slice_rows(pair));
     ptx::prefetch_tensormap(&map_a);
     ptx::prefetch_tensormap(&map_b);
     ptx::prefetch_tensormap(&map_c);
@@ -285,7 +296,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         const uint32_t remote_row = ptx::mapa(sRecv + slot * Cfg::kRecvSlotBytes + i * 16u, dst_cta);
         const uint32_t remote_bar = ptx::mapa(recv_bar, dst_cta);
 #pragma unroll 1
-        for (int c = 0; c < Cfg::kSliceRows / 32; ++c) {
+        for (int c = 0; c < slice_rows(static_cast<uint32_t>(dst_pair)) / 32; ++c) {
           uint32_t v[32];
           if (have) {
             ptx::tmem_ld_32x32b_x32(t_row + dst_pair * Cfg::kSliceRows + c * 32, v);
@@ -322,7 +333,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         ok = __all_sync(0xFFFFFFFFu, got);
       }
 #pragma unroll 1
-      for (int c = 0; c < Cfg::kSliceRows / 32; ++c) {
+      for (int c = 0; c < slice_rows(pair) / 32; ++c) {
         if (have) {
           if (c > 0 || S == 1) ptx::tmem_ld_32x32b_x32(t_row + pair * Cfg::kSliceRows + c * 32, v);
           ptx::tmem_wait_ld();

@@ -85,3 +85,25 @@ def test_python_constants_match_header():
     body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
     fields = re.findall(r"(\w+);", body)
     assert fields == [f for f, _ in _lib.Epilogue._fields_]
+
+
+def test_allgather_argument_checks_without_cuda():
+    """The fused all-gather entry points reject bad arguments before any CUDA
+    call: no multicast address, a misaligned one, N % 8 != 0, and K == 0
+    (with K == 0 the other ranks' blocks would never be written)."""
+    lib = _lib.load()
+    mc_ok, mc_bad = 0x100000, 0x100008
+    assert lib.b200gemm_bf16_nt_allgather_multicast(None, 64, 64, 64, None, None, None, 64, None,
+                                                    None) == _lib.ERR_INVALID_ARG
+    assert lib.b200gemm_bf16_nt_allgather_multicast(None, 64, 64, 64, None, None, None, 64, mc_bad,
+                                                    None) == _lib.ERR_UNSUPPORTED
+    assert lib.b200gemm_bf16_nt_allgather_multicast(None, 64, 60, 64, None, None, None, 64, mc_ok,
+                                                    None) == _lib.ERR_UNSUPPORTED
+    assert lib.b200gemm_bf16_nt_allgather_multicast(None, 64, 64, 0, None, None, None, 64, mc_ok,
+                                                    None) == _lib.ERR_UNSUPPORTED
+    assert lib.b200gemm_bf16_nt_allgather_multicast(None, 64, 64, 64, None, None, None, 64, mc_ok,
+                                                    None) == _lib.ERR_INVALID_ARG  # null handle
+    assert lib.b200gemm_bf16_nt_allgather(None, 64, 64, 0, None, None, None, 64, None, 0,
+                                          None) == _lib.ERR_UNSUPPORTED
+    assert lib.b200gemm_bf16_nt_allgather(None, 64, 64, 64, None, None, None, 64, None, 8,
+                                          None) == _lib.ERR_INVALID_ARG  # more than 7 peers
