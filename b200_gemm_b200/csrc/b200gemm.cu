@@ -34,6 +34,10 @@ namespace b200gemm {
 #ifndef B200GEMM_L2_PROMOTION
 #define B200GEMM_L2_PROMOTION 3
 #endif
+// Small-M pair kernel: allow a K split over 3 CTA pairs (129..256 rows of A).
+#ifndef B200GEMM_SMALLM_SPLIT3
+#define B200GEMM_SMALLM_SPLIT3 1
+#endif
 // Time of a 256 x 448 tile relative to a 256 x 512 tile in the width model.
 #ifndef B200GEMM_TILE448_SCALE
 #define B200GEMM_TILE448_SCALE 0.9
@@ -793,7 +797,7 @@ int decode_split(const b200gemm_handle* h, int M, int N, int K) {
   const int num_kb = (K + kBlockK - 1) / kBlockK;
   const int* fit = M > 128 ? h->decode256_clusters : h->decode_clusters;
   for (int s : {4, 3, 2}) {
-    if (s == 3 && M <= 128) continue;
+    if (s == 3 && (M <= 128 || !B200GEMM_SMALLM_SPLIT3)) continue;
     if (clusters <= fit[s] && num_kb >= 2 * s) return s;
   }
   return 1;

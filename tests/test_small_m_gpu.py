@@ -22,7 +22,8 @@ def _bits(t):
 
 
 # (M, N, K, kernel, split) on a 148-SM B200.  Pair kernel: 256 rows of B per
-# CTA pair, clusters of 2S CTAs (33 clusters of 4 and 15 of 8 fit at once);
+# CTA pair, clusters of 2S CTAs (33 clusters of 4 and 15 of 8 fit at once;
+# clusters of 6, split 3, only for 129..256 rows of A);
 # single-CTA kernel: 128 rows of B per CTA, clusters of S, taken where it
 # puts at least 1.5x the CTAs to work (narrow N).
 CASES = [
@@ -39,10 +40,11 @@ CASES = [
     (128, 8192, 8128, "small_m", 2),    # 127 K blocks: the last stage's second block lies past K
     (64, 16384, 320, "small_m", 1),     # 5 K blocks in stages of 2
     # 129..256 rows of A: the pair kernel with MMA N = 256, one K block per stage
-    (256, 4096, 1024, "small_m", 2),
+    (256, 4096, 1024, "small_m", 3),    # 16 clusters of 8 do not fit: split 3 (slices 96 + 96 + 64)
+    (160, 4096, 1032, "small_m", 3),    # split 3, ragged K; the third pair's rows all lie past M
     (192, 2048, 1000, "small_m", 4),    # ragged K
     (129, 16384, 256, "small_m", 1),
-    (200, 1032, 384, "small_m", 2),     # ragged M and N
+    (200, 1032, 384, "small_m", 3),     # ragged M and N; 6 K blocks over 3 pairs
     (256, 8192, 520, "small_m", 2),     # 9 K blocks, the last one partial
 ]
 
