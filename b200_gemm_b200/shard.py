@@ -2,9 +2,16 @@
 
 C = A . B^T splits along N into independent column blocks: rank r holds all
 of A, rows [n0, n1) of B and computes C[:, n0:n1].  No data crosses GPUs on
-the compute path.  Gathering C afterwards is optional and separate:
-`allgather_columns` runs one NCCL all-gather of the shards (shard-major
-[world][M][n_r]) and repacks it into a row-major M x N matrix.
+the compute path.  Gathering C afterwards is optional:
+  * `allgather_columns`: one NCCL all-gather of the shards (shard-major
+    [world][M][n_r]), repacked into a row-major M x N matrix;
+  * `FusedAllGather`: the GEMM's epilogue writes each finished chunk into
+    every peer's full-width C over NVLink (CUDA IPC mappings);
+  * `MulticastAllGather`: the same through one NVLink multicast mapping of
+    every rank's C (NVSwitch replicates each store).
+With operands in host memory, `ShardedHostGemm` has each rank upload only
+its share of A's rows (plus its B rows) and gathers the rest of A over
+NVLink, so the host link carries A once per node.
 
 The reference has no multi-GPU code; this module is the host logic for the
 N-sharded configurations of the benchmark (16384^3 over 1/2/4/8 GPUs, the

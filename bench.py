@@ -55,6 +55,8 @@ WORKLOADS = {
     # one GPU's part of square16384 on 8 GPUs (N = 16384 / 8 columns)
     "shard16384x8": dict(M=16384, N=2048, K=16384, dist="normal", scaling="weak"),
     "mlp": dict(M=16384, N=14336, K=4096, dist="mlp", scaling="strong"),
+    # one GPU's part of mlp on 8 GPUs (N = 14336 / 8 columns)
+    "mlp_shard8": dict(M=16384, N=1792, K=4096, dist="mlp", scaling="weak"),
     # Decode shapes run as a decoder runs them: back to back, each step on the
     # next of `weights` weight matrices (B), whose total exceeds twice L2, with
     # the small-M kernels' launch overlap (B200GEMM_PDL_WEIGHTS_EARLY).
