@@ -707,7 +707,7 @@ int tail_half_for(const b200gemm_handle* h, int tiles, int clusters) {
 }
 
 // Instances that carry the K-split tail (GemmCfg::kTailSplit): the plain
-// ones except the 512-wide, whose 16 epilogue warps leave it no registers.
+// ones with one MMA column block (not the shared-A 512- and 448-wide ones).
 bool tail_split_width(int width, bool fused) {
   return !fused && (width == 512 ? CfgN512::kTailSplit : (width == 448 ? CfgN448::kTailSplit : true));
 }
