@@ -68,3 +68,18 @@ def test_host_path_interleaved_streams(gpu_handle):
         ref = gpu_handle.bf16_nt(hA.cuda(), hB.cuda())
         torch.cuda.synchronize()
         assert torch.equal(out.view(torch.int16), ref.cpu().view(torch.int16))
+
+
+def test_host_path_ragged_vs_oracle(gpu_handle, oracle_mod):
+    """A ragged shape (M, N, K not multiples of the tile sizes) through the
+    host-buffer path, checked directly against the fp64 CPU oracle on every
+    element, |err| <= 2^-7 (|ref| + 1)."""
+    M, N, K = 1300, 904, 328
+    A_bits, B_bits = data.host_operands(M, N, K, "normal", seed=77)
+    out = torch.full((M, N), float("nan"), dtype=torch.bfloat16).pin_memory()
+    gpu_handle.bf16_nt_host(_host(A_bits, True), _host(B_bits, True), out=out)
+    torch.cuda.current_stream().synchronize()
+    got = oracle_mod.bf16_to_f32(out.view(torch.int16).numpy().view(np.uint16))
+    ref = oracle_mod.gemm_f64(A_bits, B_bits)
+    assert not np.isnan(got).any()
+    assert oracle_mod.within_tolerance(got, ref).all(), oracle_mod.max_scaled_error(got, ref)
