@@ -349,7 +349,9 @@ cudaError_t launch_gemm(int clusters, cudaStream_t stream, const CUtensorMap& ma
 // for 256.  The 512-wide tile shares one A stage between two MMAs and pays
 // its non-overlapped epilogue; fitted on 8192^3 and 16384 x 14336 x 4096
 // (where 512 wins by 9.8% and 1.3%): its K blocks run 1 / 0.8545 as fast
-// per flop as the 256-wide tile's and the epilogue costs 17 K blocks.
+// per flop as the 256-wide tile's and the epilogue costs 13 K blocks (17
+// before the accumulator read-out went ahead of the stores; with 13,
+// 16384 x 2048 x 4096 moves to 512-wide tiles, measured 2% faster).
 // `epi` adds the fused epilogue's measured per-tile cost (epilogue_cost).
 double tile_plan_cost(int width, uint32_t tiles_m, int N, int num_kb, int clusters,
                       double epi = 0.0, bool half_tail = false) {
@@ -364,7 +366,7 @@ double tile_plan_cost(int width, uint32_t tiles_m, int N, int num_kb, int cluste
   if (width == 512 || width == 448) {
     // 448: two N = 224 MMAs and 7/8 of the read-out per tile.
     const double scale = width == 448 ? B200GEMM_TILE448_SCALE : 1.0;
-    const double tile_time = scale * (2.0 * num_kb + 17.0) * 0.8545 / 0.85;
+    const double tile_time = scale * (2.0 * num_kb + 13.0) * 0.8545 / 0.85;
     const uint64_t rem = tiles % static_cast<uint64_t>(clusters);
     if (half_tail && epi == 0.0 && rem > 0 && 2 * rem <= static_cast<uint64_t>(clusters)) {
       // The last wave runs as 256-column halves on their own 4-stage ring:
