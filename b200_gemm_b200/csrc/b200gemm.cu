@@ -69,8 +69,11 @@ using CfgN192 = GemmCfg<7, 1, 192>;
 using CfgN128 = GemmCfg<8, 1, 128>;
 // The same five widths with the fused epilogue compiled in.
 using CfgE256 = GemmCfg<B200GEMM_STAGES_N256, 1, 256, true>;
-using CfgE512 = GemmCfg<4, 2, 256, true>;  // 8 epilogue warps: the fused math needs their registers
-using CfgE448 = GemmCfg<4, 2, 224, true>;
+#ifndef B200GEMM_STAGES_E512
+#define B200GEMM_STAGES_E512 4
+#endif
+using CfgE512 = GemmCfg<B200GEMM_STAGES_E512, 2, 256, true>;  // 8 epilogue warps: the fused math needs their registers
+using CfgE448 = GemmCfg<B200GEMM_STAGES_E512, 2, 224, true>;
 using CfgE224 = GemmCfg<6, 1, 224, true>;
 using CfgE192 = GemmCfg<7, 1, 192, true>;
 using CfgE128 = GemmCfg<8, 1, 128, true>;

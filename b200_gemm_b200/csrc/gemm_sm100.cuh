@@ -48,6 +48,10 @@
 #ifndef B200GEMM_CBUFS_N512
 #define B200GEMM_CBUFS_N512 4
 #endif
+// The same for the fused-epilogue shared-A instances.
+#ifndef B200GEMM_CBUFS_E512
+#define B200GEMM_CBUFS_E512 2
+#endif
 
 
 namespace b200gemm {
@@ -222,7 +226,7 @@ struct GemmCfg {
   // Staging buffers per epilogue warp: a chunk's buffer is free once the
   // TMA store issued kCBufs chunks earlier has read it (about a microsecond),
   // so more buffers let a warp drain its accumulator faster.
-  static constexpr int kCBufs = (NB == 2 && !EPI) ? B200GEMM_CBUFS_N512 : 2;
+  static constexpr int kCBufs = NB == 2 ? (EPI ? B200GEMM_CBUFS_E512 : B200GEMM_CBUFS_N512) : 2;
   // Plain instances with one accumulator: every epilogue warp reads all its
   // chunks from TMEM before any TMA store, the first kCBufs into its staging
   // buffers and the rest into registers, so the accumulator is released
