@@ -1237,6 +1237,10 @@ int gemm_device(b200gemm_t h, int M, int N, int K, const void* A, const void* B,
     clusters = p.num_units < max_clusters ? p.num_units : max_clusters;
   }
 
+  // One wave of whole tiles: each cluster computes its tile from its index
+  // instead of loading it from the table (a dependent global load before
+  // the first operand load, which matters for small, latency-bound calls).
+  if (p.num_units == p.num_tiles && p.num_tiles <= clusters) p.direct_tiles_n = static_cast<int>(tiles_n);
   const cudaError_t e = launch_width(width, fused, clusters, stream, ma, mb, mc, p);
   if (e == cudaSuccess && tail_on) {
     std::lock_guard<std::mutex> lock(h->mu);

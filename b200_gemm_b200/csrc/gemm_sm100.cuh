@@ -81,6 +81,10 @@ struct GemmParams {
   int num_kb;                 // ceil(K / kBlockK)
   int num_tiles;              // ceil(M / 256) * ceil(N / tile width)
   const uint32_t* tiles;      // schedule: num_tiles packed (tm << 16 | tn) in start order
+  // Single-wave grids (every tile starts at once, so the order is moot):
+  // whole tile u is (u / direct_tiles_n, u % direct_tiles_n), computed
+  // instead of loaded from `tiles`; 0 = use the table.
+  int direct_tiles_n;
   unsigned int* status;       // 4 status words (code, site, cta, tile); may be null
   unsigned long long timeout_ns;
   uint16_t* C;                // C base (bf16 bits), for the ragged-N edge chunk
@@ -153,7 +157,9 @@ template <bool HALF>
 __device__ __forceinline__ WorkUnit unit_at(const GemmParams& p, uint32_t u) {
   WorkUnit w;
   if (u < static_cast<uint32_t>(p.tail_start)) {
-    w.tile = __ldg(p.tiles + u);
+    w.tile = p.direct_tiles_n > 0
+                 ? ((u / static_cast<uint32_t>(p.direct_tiles_n)) << 16) | (u % static_cast<uint32_t>(p.direct_tiles_n))
+                 : __ldg(p.tiles + u);
     w.kb_begin = 0;
     w.kb_end = p.num_kb;
     w.slot = -1;
