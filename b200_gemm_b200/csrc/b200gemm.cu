@@ -34,6 +34,11 @@ namespace b200gemm {
 #ifndef B200GEMM_L2_PROMOTION
 #define B200GEMM_L2_PROMOTION 3
 #endif
+// Small-M pair kernel over 128- or 256-row blocks of A for small shapes of up
+// to this many rows (256 = never above 256 rows).
+#ifndef B200GEMM_SMALLM_MAX_ROWS
+#define B200GEMM_SMALLM_MAX_ROWS 4096
+#endif
 // Small-M pair kernel: allow a K split over 3 CTA pairs (129..256 rows of A).
 #ifndef B200GEMM_SMALLM_SPLIT3
 #define B200GEMM_SMALLM_SPLIT3 1
@@ -302,7 +307,8 @@ cudaError_t launch_smallm1(cudaStream_t stream, const CUtensorMap& ma, const CUt
 template <class Cfg>
 cudaError_t launch_decode(cudaStream_t stream, const CUtensorMap& ma, const CUtensorMap& mb,
                           const CUtensorMap& mc, const CUtensorMap& mr, const DecodeParams& p) {
-  const unsigned clusters = static_cast<unsigned>((p.N + 255) / 256);
+  const unsigned clusters =
+      static_cast<unsigned>(p.n_blocks) * static_cast<unsigned>((p.M + Cfg::kNT - 1) / Cfg::kNT);
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -824,6 +830,8 @@ uint32_t decode_slice_rows(int nt, int split) {
 struct SmallMPlan {
   int kind;
   int split;
+  int nt = 0;        // pair kernel: rows of A per MMA (128 or 256)
+  int clusters = 0;  // clusters launched
 };
 
 // Device-side epilogue arguments of a call (identity when epi is null).
@@ -873,21 +881,70 @@ bool encode_smallm_c(CUtensorMap* mc, void* C, int M, int N, int ldc, uint32_t s
                        : (u8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16));
 }
 
-SmallMPlan smallm_plan(const b200gemm_handle* h, int M, int N, int K) {
+// 257..B200GEMM_SMALLM_MAX_ROWS rows of A: the pair kernel over blocks of
+// 128 or 256 rows of A (clusters = N / 256 x M / block, K split over 2 or 4
+// pairs, so every slice is whole 32-row chunks inside its block).  All its
+// clusters must fit at once.  Measured on B200, both kernels are then bound
+// by how fast each CTA is fed from L2 (~12-15 ns per KB); so the first
+// layout that fits -- 128-row blocks before 256-row ones (their smaller
+// partial sums cost less to exchange), split 4 where every pair gets at
+// least 4 K blocks -- is taken where a CTA's bytes (operand K blocks plus
+// the partial sums it exchanges) are at most 0.8 of what a CTA of the tiled
+// kernel loads (waves x K blocks x (16 + width / 16) KB).  {0, 0} otherwise,
+// and while a tile width is forced (that asks for the tiled kernel).
+SmallMPlan smallm_blocks_plan(const b200gemm_handle* h, int M, int N, int K, const b200gemm_epilogue* epi) {
+  if (h->tile_width != 0 || M <= 256 || M > B200GEMM_SMALLM_MAX_ROWS || (N % 8) != 0 || K < 2 * kBlockK) return {0, 0};
+  const int num_kb = (K + kBlockK - 1) / kBlockK;
+  const int n_blocks = (N + 255) / 256;
+  SmallMPlan pick{0, 0};
+  double pair_kb = 0.0;  // KB one CTA loads and exchanges
+  for (int nt : {128, 256}) {
+    const int clusters = n_blocks * ((M + nt - 1) / nt);
+    const int* fit = nt == 256 ? h->decode256_clusters : h->decode_clusters;
+    for (int s : {4, 2}) {
+      if (clusters > fit[s] || num_kb < (s == 4 ? 16 : 4)) continue;
+      pick = SmallMPlan{2, s};
+      pick.nt = nt;
+      pick.clusters = clusters;
+      pair_kb = ((num_kb + s - 1) / s) * (16.0 + nt / 16.0) + nt / 2.0 * (s - 1) / s;
+      break;
+    }
+    if (pick.kind != 0) break;
+  }
+  if (pick.kind == 0) return pick;
+  const int width = choose_tile_width(h, M, N, K, epi);
+  const int wi = width_index(width);
+  const int maxc = epi != nullptr ? h->clusters_epi[wi] : h->clusters_w[wi];
+  const int tiles = ((M + kTileM - 1) / kTileM) * ((N + width - 1) / width);
+  const int waves = (tiles + maxc - 1) / maxc;
+  const double tiled_kb = static_cast<double>(waves) * num_kb * (16.0 + width / 16.0);
+  if (pair_kb > 0.8 * tiled_kb) return {0, 0};
+  return pick;
+}
+
+SmallMPlan smallm_plan(const b200gemm_handle* h, int M, int N, int K, const b200gemm_epilogue* epi = nullptr) {
+  if (M > 256) return smallm_blocks_plan(h, M, N, K, epi);
   const int sp = decode_split(h, M, N, K);
   if (sp == 0) return {0, 0};
-  if (M > 128) return {2, sp};  // the single-CTA kernel covers at most 128 rows of A
+  SmallMPlan pair{2, sp};
+  pair.nt = M > 128 ? 256 : 128;
+  pair.clusters = (N + 255) / 256;
+  if (M > 128) return pair;  // the single-CTA kernel covers at most 128 rows of A
   const int ctas_pair = (N + 255) / 256 * 2 * sp;
   const int clusters1 = (N + 127) / 128;
   const int num_kb = (K + kBlockK - 1) / kBlockK;
   for (int s : {4, 2}) {  // (without a K split it never has 1.5x the pair kernel's CTAs)
     if (clusters1 <= h->smallm1_clusters[s] && num_kb >= 2 * s) {
       const int ctas_single = clusters1 * s;
-      if (2 * ctas_single >= 3 * ctas_pair && ctas_single <= h->sm_count) return {3, s};
+      if (2 * ctas_single >= 3 * ctas_pair && ctas_single <= h->sm_count) {
+        SmallMPlan one{3, s};
+        one.clusters = clusters1;
+        return one;
+      }
       break;
     }
   }
-  return {2, sp};
+  return pair;
 }
 
 int run_smallm1(b200gemm_t h, int split, int M, int N, int K, const void* A, const void* B, void* C,
@@ -920,12 +977,11 @@ int run_smallm1(b200gemm_t h, int split, int M, int N, int K, const void* A, con
   return e == cudaSuccess ? B200GEMM_OK : B200GEMM_ERR_CUDA;
 }
 
-int run_decode(b200gemm_t h, int split, int M, int N, int K, const void* A, const void* B, void* C,
-               int ldc, cudaStream_t stream, unsigned long long timeout_ns, int pdl,
+int run_decode(b200gemm_t h, int split, int nt, int M, int N, int K, const void* A, const void* B,
+               void* C, int ldc, cudaStream_t stream, unsigned long long timeout_ns, int pdl,
                const b200gemm_epilogue* epi) {
   const uint64_t k = static_cast<uint64_t>(K);
-  CUtensorMap ma, mb, mc, mr;
-  const int nt = M > 128 ? 256 : 128;  // rows of A one MMA covers
+  CUtensorMap ma, mb, mc, mr;  // nt: rows of A one MMA covers (one M block)
   const uint32_t slice_rows = decode_slice_rows(nt, split);
   const EpiArgs ea = epi_args(epi);
   if (!encode_2d(&ma, A, k, static_cast<uint64_t>(M), k * 2, kBlockK, nt / 2, CU_TENSOR_MAP_SWIZZLE_128B) ||
@@ -946,6 +1002,7 @@ int run_decode(b200gemm_t h, int split, int M, int N, int K, const void* A, cons
   p.status = h->status_dev;
   p.timeout_ns = timeout_ns;
   p.pdl = pdl;
+  p.n_blocks = (N + 255) / 256;
   cudaError_t e;
   if (nt == 256) {
     if (split == 4) e = launch_decode<DecodeCfg<4, 256>>(stream, ma, mb, mc, mr, p);
@@ -1122,11 +1179,11 @@ int gemm_device(b200gemm_t h, int M, int N, int K, const void* A, const void* B,
                          (c_type != B200GEMM_OUT_E4M3 || (N % 16) == 0);
   {
     std::lock_guard<std::mutex> lock(h->mu);
-    if (smallm_ok && h->small_m != 0) sm = smallm_plan(h, M, N, K);
+    if (smallm_ok && h->small_m != 0) sm = smallm_plan(h, M, N, K, epi);
     decode_timeout = h->timeout_ns;
     pdl = h->pdl;
   }
-  if (sm.kind == 2) return run_decode(h, sm.split, M, N, K, A, B, C, ldc, stream, decode_timeout, pdl, epi);
+  if (sm.kind == 2) return run_decode(h, sm.split, sm.nt, M, N, K, A, B, C, ldc, stream, decode_timeout, pdl, epi);
   if (sm.kind == 3) return run_smallm1(h, sm.split, M, N, K, A, B, C, ldc, stream, decode_timeout, pdl, epi);
 
   CUtensorMap ma, mb, mc;
@@ -1260,8 +1317,8 @@ extern "C" int b200gemm_plan(b200gemm_t h, int M, int N, int K, int* plan) {
   if (sm.kind != 0) {
     plan[0] = sm.kind;  // 2: small-M pair kernel, 3: small-M single-CTA kernel
     plan[1] = sm.kind == 2 ? 256 : 128;  // rows of B per cluster
-    plan[2] = (N + plan[1] - 1) / plan[1];
-    plan[3] = plan[2];
+    plan[2] = sm.clusters;
+    plan[3] = sm.clusters;
     plan[5] = sm.split;
     return B200GEMM_OK;
   }

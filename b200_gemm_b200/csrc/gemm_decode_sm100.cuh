@@ -18,6 +18,11 @@
 // of that slice, adds them, rounds to bf16 and writes C through a transposing
 // staging buffer.  No global workspace, one launch, N/256 * 2S CTAs.
 //
+// Small shapes with more rows of A (up to a few thousand, few output tiles)
+// run the same kernel over blocks of NT rows of A: one cluster per 256 rows
+// of B x NT rows of A, N/256 * M/NT clusters, so K splits across the CTA
+// pairs where the tiled kernel's few tiles would leave most SMs idle.
+//
 // Reference path: b200_kernels/matmul_1.cuh:329-418 computes the same C with
 // 256 x 256 tiles only; decode shapes are a BASELINE configuration the
 // reference does not specialise.
@@ -40,6 +45,11 @@ struct DecodeParams {
   unsigned long long timeout_ns;
   EpiArgs epi;       // fused epilogue (identity: no flags, act none, bf16, alpha 1)
   int pdl;           // launch overlap with the previous kernel: kPdl*
+  // Clusters are laid out [M block][N block]: cluster c covers rows of B
+  // (columns of C) from 256 (c % n_blocks) and rows of A (rows of C) from
+  // NT (c / n_blocks).  More than one M block (M > NT) needs slices that end
+  // inside their block: split 1, 2 or 4.
+  int n_blocks;      // ceil(N / 256)
 };
 
 // NT = rows of A covered (the MMA's N): 128 for M <= 128, 256 for M <= 256.
@@ -123,7 +133,8 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     return pr + 1 == static_cast<uint32_t>(S) ? Cfg::kLastSliceRows : Cfg::kSliceRows;
   };
   const bool leader = half == 0;
-  const int n0 = static_cast<int>(ptx::cluster_id_x()) * 256;
+  const int n0 = static_cast<int>(ptx::cluster_id_x() % static_cast<uint32_t>(p.n_blocks)) * 256;
+  const int m0 = static_cast<int>(ptx::cluster_id_x() / static_cast<uint32_t>(p.n_blocks)) * Cfg::kNT;
   const int kb_begin = static_cast<int>(pair) * p.kb_per_split;
   const int kb_end = min(p.num_kb, kb_begin + p.kb_per_split);
   const int nkb = kb_end > kb_begin ? kb_end - kb_begin : 0;
@@ -181,7 +192,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       // Each stage covers K blocks [kb, kb + KPS); the pair's range is a whole
       // number of stages (a block past K reads as zeros).
       constexpr int KPS = Cfg::kKps;
-      const int brow = n0 + static_cast<int>(half) * 128, arow = static_cast<int>(half) * (Cfg::kNT / 2);
+      const int brow = n0 + static_cast<int>(half) * 128, arow = m0 + static_cast<int>(half) * (Cfg::kNT / 2);
       const int nst = (nkb + KPS - 1) / KPS;
       const int pre = p.pdl == kPdlWeightsEarly ? min(STAGES, nst) : 0;
       for (int s = 0; s < pre; ++s) {
@@ -277,7 +288,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     // The residual rows and columns this warp adds at the end: one TMA load
     // into the B stages (free once the MMAs are done), in flight during the
     // exchange below.  Rows past M and columns past N read as zeros.
-    const int row0 = static_cast<int>(pair) * Cfg::kSliceRows;
+    const int row0 = m0 + static_cast<int>(pair) * Cfg::kSliceRows;
     const int col = n0 + static_cast<int>(half) * 128 + static_cast<int>(quarter) * 32;
     const uint32_t res_bar = base + Cfg::kResBar + 8 * (warp - 2u);
     const uint32_t rtile = sC + 4 * Cfg::kCWarpBytes + (warp - 2u) * Cfg::kRWarpBytes;

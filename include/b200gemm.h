@@ -85,7 +85,7 @@ typedef struct b200gemm_epilogue {
 /* C = epilogue(A . B^T) with the epilogue above; epi == NULL is exactly
  * b200gemm_bf16_nt.  Same rules as b200gemm_bf16_nt, plus K > 0 and those in
  * the struct.  Runs the kernel b200gemm_bf16_nt would run for the shape (the
- * small-M kernels for M <= 256, except e4m3 output with N % 16 != 0); the
+ * small-M kernels where it would, except e4m3 output with N % 16 != 0); the
  * tiled kernel's width accounts for the epilogue's cost (a costly epilogue
  * favours 256-wide tiles, whose epilogue overlaps the next tile's MMAs).
  * Every tile width sums an element's K products in the same order, so the
@@ -223,9 +223,13 @@ int b200gemm_tile_width_for(b200gemm_t handle, int M, int N, int K);
  * MMA's M side and K is split over 1, 2 or 4 CTA pairs of one cluster whose
  * fp32 partial sums are reduced through distributed shared memory, so every
  * SM streams B from HBM.  The CTA-pair form covers up to 256 rows of A, the
- * single-CTA form up to 128.  mode -1 (default) or 1: use them for eligible
- * shapes; 0: always use the tiled kernel.  The reference has no small-M
- * path. */
+ * single-CTA form up to 128.  The CTA-pair form also runs small shapes of
+ * 257..4096 rows of A (N % 8 == 0, K >= 256 split over 2 or 4 pairs) over
+ * blocks of 128 or 256 rows of A, one cluster per block of B and A rows,
+ * where all clusters fit at once and each CTA then loads fewer bytes than a
+ * CTA of the tiled kernel would; never while a tile width is forced.
+ * mode -1 (default) or 1: use them for eligible shapes; 0: always use the
+ * tiled kernel.  The reference has no small-M path. */
 int b200gemm_set_small_m(b200gemm_t handle, int mode);
 
 /* Launch overlap with the previous kernel (programmatic dependent launch).
@@ -237,7 +241,7 @@ int b200gemm_set_small_m(b200gemm_t handle, int mode);
  * WEIGHTS_EARLY: as ON, and the first ring of B (the weights) is requested
  *   before that wait, so streaming B overlaps the previous kernel's tail.
  *   The caller guarantees that the previous kernel does not write B.
- * The tiled kernel (M > 256) takes WEIGHTS_EARLY as ON: it reads its tile
+ * The tiled kernel takes WEIGHTS_EARLY as ON: it reads its tile
  * table before any operand.  The multi-GPU all-gather form never overlaps.
  * Work on the stream other than these kernels (copies, events, other
  * kernels) keeps plain stream order.  The reference launches one kernel per

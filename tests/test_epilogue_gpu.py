@@ -96,7 +96,7 @@ def test_epilogue_terms_and_widths(gpu_handle, oracle_mod, use_bias, use_res, wi
 # (M, N, K, small-M kernel the plan picks)
 SMALL_M = [(1, 1024, 512, "small_m"), (64, 4096, 1024, "small_m_1cta"), (128, 8192, 512, "small_m"),
            (77, 1040, 384, "small_m"), (100, 3968, 704, "small_m_1cta"), (256, 4096, 512, "small_m"),
-           (200, 1040, 384, "small_m")]
+           (200, 1040, 384, "small_m"), (640, 1024, 512, "small_m"), (2048, 1024, 2048, "small_m")]
 
 
 @pytest.mark.parametrize("M,N,K,kernel", SMALL_M)

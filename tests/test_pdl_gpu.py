@@ -16,8 +16,10 @@ torch = pytest.importorskip("torch")
 
 MODES = [_lib.PDL_ON, _lib.PDL_WEIGHTS_EARLY]
 # (M, K = N, plan kernel): the pair kernel, the single-CTA kernel, the tiled
-# kernel, the pair kernel covering 256 rows of A
-CHAINS = [(128, 8192, "small_m"), (96, 4096, "small_m_1cta"), (512, 4096, "tiled"), (256, 4096, "small_m")]
+# kernel, the pair kernel covering 256 rows of A, the pair kernel over two
+# 256-row blocks of A
+CHAINS = [(128, 8192, "small_m"), (96, 4096, "small_m_1cta"), (1024, 4096, "tiled"), (256, 4096, "small_m"),
+          (512, 4096, "small_m")]
 STEPS = 6
 
 

@@ -23,7 +23,8 @@ def _bits(t):
 
 # (M, N, K, kernel, split) on a 148-SM B200.  Pair kernel: 256 rows of B per
 # CTA pair, clusters of 2S CTAs (33 clusters of 4 and 15 of 8 fit at once;
-# clusters of 6, split 3, only for 129..256 rows of A);
+# clusters of 6, split 3, only for 129..256 rows of A; above 256 rows of A
+# a cluster covers 128 or 256 of them, split 2 or 4);
 # single-CTA kernel: 128 rows of B per CTA, clusters of S, taken where it
 # puts at least 1.5x the CTAs to work (narrow N).
 CASES = [
@@ -46,6 +47,17 @@ CASES = [
     (129, 16384, 256, "small_m", 1),
     (200, 1032, 384, "small_m", 3),     # ragged M and N; 6 K blocks over 3 pairs
     (256, 8192, 520, "small_m", 2),     # 9 K blocks, the last one partial
+    # More than 256 rows of A: one cluster per 256 rows of B x 128 (or 256)
+    # rows of A, where a CTA then moves at most 0.8x the tiled kernel's bytes.
+    (512, 512, 512, "small_m", 2),      # 8 K blocks: too few for split 4
+    (384, 512, 2048, "small_m", 4),     # 6 clusters of 8
+    (1024, 1024, 1024, "small_m", 2),   # 32 clusters of 4
+    (1000, 1024, 1000, "small_m", 2),   # ragged M and K: the last M block is 104 rows
+    (768, 1032, 384, "small_m", 2),     # ragged N; 6 K blocks over 2 pairs
+    (2048, 1024, 4096, "small_m", 2),   # 256-row blocks of A: 32 clusters of 4
+    (2000, 1000, 4000, "small_m", 2),   # 256-row blocks, ragged M, N and K
+    (300, 1024, 136, "tiled", 0),       # 3 K blocks: too few to split
+    (4096, 512, 512, "tiled", 0),       # the tiled kernel moves fewer bytes per CTA
 ]
 
 
