@@ -891,8 +891,10 @@ bool encode_smallm_c(CUtensorMap* mc, void* C, int M, int N, int ldc, uint32_t s
 // least 4 K blocks -- is taken where a CTA's bytes (operand K blocks plus
 // the partial sums it exchanges) are at most 0.8 of what a CTA of the tiled
 // kernel loads (waves x K blocks x (16 + width / 16) KB).  {0, 0} otherwise,
-// and while a tile width is forced (that asks for the tiled kernel).
-SmallMPlan smallm_blocks_plan(const b200gemm_handle* h, int M, int N, int K, const b200gemm_epilogue* epi) {
+// and while a tile width is forced (that asks for the tiled kernel).  A fused
+// epilogue does not change the choice: such a call runs the kernel the plain
+// call runs.
+SmallMPlan smallm_blocks_plan(const b200gemm_handle* h, int M, int N, int K) {
   if (h->tile_width != 0 || M <= 256 || M > B200GEMM_SMALLM_MAX_ROWS || (N % 8) != 0 || K < 2 * kBlockK) return {0, 0};
   const int num_kb = (K + kBlockK - 1) / kBlockK;
   const int n_blocks = (N + 255) / 256;
@@ -912,9 +914,8 @@ SmallMPlan smallm_blocks_plan(const b200gemm_handle* h, int M, int N, int K, con
     if (pick.kind != 0) break;
   }
   if (pick.kind == 0) return pick;
-  const int width = choose_tile_width(h, M, N, K, epi);
-  const int wi = width_index(width);
-  const int maxc = epi != nullptr ? h->clusters_epi[wi] : h->clusters_w[wi];
+  const int width = choose_tile_width(h, M, N, K);
+  const int maxc = h->clusters_w[width_index(width)];
   const int tiles = ((M + kTileM - 1) / kTileM) * ((N + width - 1) / width);
   const int waves = (tiles + maxc - 1) / maxc;
   const double tiled_kb = static_cast<double>(waves) * num_kb * (16.0 + width / 16.0);
@@ -922,8 +923,8 @@ SmallMPlan smallm_blocks_plan(const b200gemm_handle* h, int M, int N, int K, con
   return pick;
 }
 
-SmallMPlan smallm_plan(const b200gemm_handle* h, int M, int N, int K, const b200gemm_epilogue* epi = nullptr) {
-  if (M > 256) return smallm_blocks_plan(h, M, N, K, epi);
+SmallMPlan smallm_plan(const b200gemm_handle* h, int M, int N, int K) {
+  if (M > 256) return smallm_blocks_plan(h, M, N, K);
   const int sp = decode_split(h, M, N, K);
   if (sp == 0) return {0, 0};
   SmallMPlan pair{2, sp};
@@ -1179,7 +1180,7 @@ int gemm_device(b200gemm_t h, int M, int N, int K, const void* A, const void* B,
                          (c_type != B200GEMM_OUT_E4M3 || (N % 16) == 0);
   {
     std::lock_guard<std::mutex> lock(h->mu);
-    if (smallm_ok && h->small_m != 0) sm = smallm_plan(h, M, N, K, epi);
+    if (smallm_ok && h->small_m != 0) sm = smallm_plan(h, M, N, K);
     decode_timeout = h->timeout_ns;
     pdl = h->pdl;
   }
@@ -1499,9 +1500,19 @@ extern "C" int b200gemm_bf16_nt_host(b200gemm_t h, int M, int N, int K, const vo
     return B200GEMM_ERR_CUDA;
   }
   st.next ^= 1;
+  // Shapes the small-M kernel takes (M <= 256, or a small shape it covers in
+  // blocks of A's rows) run as one GEMM after one upload of A, so that the
+  // result is the device path's bit for bit: the tiled kernel sums an
+  // element's K products in the same order whatever rows a chunk holds, the
+  // small-M kernel's K split does not.
+  bool whole = M <= 256;
+  if (!whole) {
+    std::lock_guard<std::mutex> plan_lock(h->mu);
+    whole = h->small_m != 0 && smallm_plan(h, M, N, K).kind != 0;
+  }
   // Chunks: whole 256-row tiles, at most kMaxChunks of them, about 8 when M allows.
   const int tiles_m = (M + kTileM - 1) / kTileM;
-  const int want = tiles_m < 8 ? tiles_m : 8;
+  const int want = whole ? 1 : (tiles_m < 8 ? tiles_m : 8);
   const int chunk_tiles = (tiles_m + want - 1) / want;
   const int chunk_rows = chunk_tiles * kTileM;
   const int chunks = (M + chunk_rows - 1) / chunk_rows;
@@ -1538,7 +1549,7 @@ extern "C" int b200gemm_bf16_nt_host(b200gemm_t h, int M, int N, int K, const vo
           !ok(cudaStreamWaitEvent(st.s_mma, st.ev_a[i], 0)))
         return B200GEMM_ERR_CUDA;
       const int rc = gemm_device(h, rows, N, K, dA + a_off, buf.dB, dC + r0 * ldc_dev * 2,
-                                 static_cast<int>(ldc_dev), st.s_mma, /*allow_small_m=*/M <= 256);
+                                 static_cast<int>(ldc_dev), st.s_mma, /*allow_small_m=*/whole);
       if (rc != B200GEMM_OK) return rc;
       if (!ok(cudaEventRecord(st.ev_c[i], st.s_mma)) ||
           !ok(cudaStreamWaitEvent(st.s_d2h, st.ev_c[i], 0)) ||

@@ -1,8 +1,9 @@
 """Fused GEMM + all-gather across GPUs (b200gemm_bf16_nt_allgather): every
 rank computes its column block of C and its epilogue writes the block into
 every rank's full-width C over NVLink.  After a barrier each rank's C must
-equal, bit for bit, the single-GPU result of the whole GEMM (same kernel,
-same per-element K order).  Needs two or more GPUs; one process per GPU."""
+equal, bit for bit, the single-GPU result of the whole GEMM with the tiled
+kernel (the kernel the all-gather entry points run: same per-element K
+order).  Needs two or more GPUs; one process per GPU."""
 import os
 import socket
 
@@ -11,6 +12,17 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 torch = pytest.importorskip("torch")
+
+
+def _tiled_reference(gemm, A, B):
+    """The whole GEMM on one GPU with the tiled kernel (small-M kernel off)."""
+    gemm.set_small_m(0)
+    try:
+        full = gemm.bf16_nt(A, B)
+        torch.cuda.synchronize()
+    finally:
+        gemm.set_small_m(-1)
+    return full
 
 
 def _free_port():
@@ -45,8 +57,7 @@ def _worker(rank, world, port, M, N, K, width, q):
         rc = fused.run(A, B_local, torch.cuda.current_stream().cuda_stream)
         torch.cuda.synchronize()
         dist.barrier()
-        full = gemm.bf16_nt(A, B)
-        torch.cuda.synchronize()
+        full = _tiled_reference(gemm, A, B)
         same = bool(torch.equal(fused.view().contiguous().view(torch.int16), full.contiguous().view(torch.int16)))
         if same and rank == 0 and M * N * K <= 600 * 1536 * 264:
             # the gathered C of a ragged shape, directly against the fp64 oracle
@@ -114,7 +125,7 @@ def _mc_worker(rank, world, port, M, N, K, q):
     fused = None
     try:
         A, B = data.device_operands(M, N, K, "normal", seed=13, device=f"cuda:{rank}")
-        full = gemm.bf16_nt(A, B)
+        full = _tiled_reference(gemm, A, B)
         try:
             fused = shard.MulticastAllGather(gemm, M, N)
         except RuntimeError as e:
