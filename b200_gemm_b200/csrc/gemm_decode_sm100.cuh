@@ -24,7 +24,7 @@
 // pairs where the tiled kernel's few tiles would leave most SMs idle.
 //
 // Reference path: b200_kernels/matmul_1.cuh:329-418 computes the same C with
-// 256 x 256 tiles only; decode shapes are a BASELINE configuration the
+// 256 x 256 tiles only; decode shapes are a benchmark configuration the
 // reference does not specialise.
 #pragma once
 

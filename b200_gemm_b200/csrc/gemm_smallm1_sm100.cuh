@@ -17,7 +17,7 @@
 // slice, rounds to bf16 and writes C through a transposing staging buffer.
 //
 // Reference path: b200_kernels/matmul_1.cuh:329-418 computes the same C with
-// 256 x 256 tiles only; decode shapes are a BASELINE configuration the
+// 256 x 256 tiles only; decode shapes are a benchmark configuration the
 // reference does not specialise.
 #pragma once
 

@@ -104,7 +104,7 @@ def test_small_m_unsplit_matches_tiled_bitwise(gpu_handle, M):
 
 
 def test_decode_config_vs_cublaslt(gpu_handle, oracle_mod):
-    """BASELINE decode config 128 x 8192 x 8192: every element vs cuBLASLt,
+    """The decode benchmark configuration 128 x 8192 x 8192: every element vs cuBLASLt,
     one full row vs the fp64 oracle."""
     M, N, K = 128, 8192, 8192
     A, B = data.device_operands(M, N, K, "normal", seed=7)
