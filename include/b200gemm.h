@@ -97,8 +97,8 @@ int b200gemm_bf16_nt_epilogue(b200gemm_t handle, int M, int N, int K, const void
 /* C = A . B^T with A, B and C in host memory (pinned memory lets the copies
  * overlap; pageable memory works but serialises).  The handle stages the
  * operands in device buffers it owns (allocated on first use, grown when
- * needed): B is copied first, then A and C move in row chunks of whole
- * 256-row tiles on separate streams, so the copy of chunk i+1, the GEMM of
+ * needed): B is copied first, then A and C move in (about 3) row chunks of
+ * whole 256-row tiles on separate streams, so the copy of chunk i+1, the GEMM of
  * chunk i and the copy-out of chunk i-1 overlap.  Asynchronous with respect
  * to the host: completion is ordered on `stream`, and the host buffers must
  * stay valid until then.  Consecutive calls alternate between two sets of
