@@ -37,9 +37,12 @@
 #include "ptx_sm100.cuh"
 
 // L2 eviction priority of the operand loads (0 normal, 1 evict_last,
-// 2 evict_first); build-time tuning knobs.
+// 2 evict_first); build-time tuning knobs.  Both operands evict_last: the
+// C tiles the epilogue writes then leave L2 before A or B lines do (measured
+// 0.3-0.8% faster than A normal across 8192^3, the MLP shapes and 16384 x
+// 2048 x 16384, with the same DRAM bytes).
 #ifndef B200GEMM_L2_POLICY_A
-#define B200GEMM_L2_POLICY_A 0
+#define B200GEMM_L2_POLICY_A 1
 #endif
 #ifndef B200GEMM_L2_POLICY_B
 #define B200GEMM_L2_POLICY_B 1
