@@ -1,8 +1,9 @@
 """Parity of the small-M (decode-shaped) kernels: rows of B on the MMA's M
-side, K split over 1, 2 or 4 CTA pairs (pair kernel) or CTAs (single-CTA
-kernel) of a cluster, partial sums reduced through distributed shared memory.  Compared with the fp64 oracle
-(|err| <= 2^-7 (|ref| + 1)) and, bit for bit where the K split is 1, with the
-tiled kernel."""
+side, K split over 1, 2, 3 or 4 CTA pairs (pair kernel) or 1, 2 or 4 CTAs
+(single-CTA kernel) of a cluster, partial sums reduced through distributed
+shared memory; above 256 rows of A the pair kernel runs over blocks of 128 or
+256 rows of A.  Compared with the fp64 oracle (|err| <= 2^-7 (|ref| + 1))
+and, bit for bit where the K split is 1, with the tiled kernel."""
 import numpy as np
 import pytest
 
